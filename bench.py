@@ -1,0 +1,500 @@
+"""Benchmark: W4A16 GEMV HBM throughput on the Qwen2.5 decode projections, B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-per-shape] [--no-cpu]
+
+A step is one decode pass (M = 1) over every projection of Qwen2.5-0.5B, 1.5B and 3B: q, k, v, o, gate, up,
+down -- 21 GEMV calls. Weights are cold: the step cycles through enough distinct copies of the 21 weights
+(>= 1 GiB, 8x the 126 MB L2) that every call reads its weights from HBM. The metric is the reference's
+effective bandwidth (bench/gpu_run.py:255,267): bytes = N*K/2 + 2*N*K/128 + 2*(M*K + M*N) per call, divided
+by time.
+
+  value   whole-job GB/s with everything resident in HBM: K steps captured as CUDA graphs (one kernel launch per
+          call, programmatic dependent launch between them), timed with CUDA events on the launching stream,
+          max over ranks;
+  e2e     the same metric through the public API (lowbit.ops.linear), eager, with each call's activation copied
+          from pinned host memory to the GPU and its output copied back inside the timed region;
+  cpu_baseline / --impl reference
+          the reference's CPU path (dequantize on CPU tensors + fp32 F.linear, lowbit/ops.py:119-123) restated in
+          oracle/oracle.py, timed on the host cores of this machine.
+
+Under torchrun (--gpus N > 1) each rank runs the same sweep on its own GPU (the single-layer benchmark has no
+exchange step: replicas, weak scaling); value sums all ranks' bytes over the slowest rank's time.
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for p in (ROOT / "lowbit-kernels_b200", ROOT):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "W4A16 GEMV HBM GB/s (% of ~8 TB/s) at M=1-64; Qwen2.5-3B decode tok/s"
+MODELS = {  # hidden, intermediate, q width, kv width
+    "qwen2.5-0.5b": (896, 4864, 896, 128),
+    "qwen2.5-1.5b": (1536, 8960, 1536, 256),
+    "qwen2.5-3b": (2048, 11008, 2048, 256),
+}
+GROUP = 128
+ROTATION_BYTES = 1 << 30
+L2_BYTES = 126 * 10 ** 6
+FALLBACK_HBM_GBS = 6650.0
+
+
+def projections():
+    """[(model, proj, K, N)] in decode order."""
+    out = []
+    for name, (h, inter, q, kv) in MODELS.items():
+        out += [(name, "q", h, q), (name, "k", h, kv), (name, "v", h, kv), (name, "o", q, h),
+                (name, "gate", h, inter), (name, "up", h, inter), (name, "down", inter, h)]
+    return out
+
+
+def call_bytes(k, n, m=1):
+    return n * k // 2 + 2 * n * (k // GROUP) + 2 * (m * k + m * n)
+
+
+def rank_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peak():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        if d.get("hbm_gbs"):
+            return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy read+write)"
+    return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if one exists."""
+    f = ROOT / "profiles" / "gemv_mma_m1_sweep.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """SM clock, power and throttle reasons sampled through NVML in a thread (~10 ms period)."""
+
+    REASONS = {  # NVML clocks-event reason bits
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index):
+        self.samples, self.stop_evt, self.ok = [], threading.Event(), False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable, the bench still runs
+            self.err = str(e)
+
+    def _run(self):
+        while not self.stop_evt.is_set():
+            self.sample()
+            time.sleep(0.01)
+
+    def sample(self):
+        try:
+            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            reasons = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.samples.append((time.perf_counter(), mhz, reasons))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def __enter__(self):
+        if self.ok:
+            self.sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self.stop_evt.set()
+            self.t.join()
+            self.sample()
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"unavailable": getattr(self, "err", "nvml")}
+        win = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-2:]
+        mhz = [s[1] for s in win]
+        bits = 0
+        for s in win:
+            bits |= s[2]
+        reasons = [v for k, v in self.REASONS.items() if bits & k and v != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(win), "source": "nvml, ~10 ms period, during the timed region"}
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+
+def build_sets(ops, quant, device, n_sets, seed=0):
+    """n_sets independent copies of the 21 projection weights (mma layout only, as a model keeps them)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    sets = []
+    for _ in range(n_sets):
+        layer = []
+        for _, _, k, n in projections():
+            w = torch.randn(n, k, device=device, generator=gen) * 0.02
+            packed, scales = ops.quantize_w4_gpu(w, GROUP)
+            layer.append(ops.W4Weight(packed, scales, GROUP, ("mma",)))
+            del w, packed
+        sets.append(layer)
+    return sets
+
+
+def capture(fn):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(g):
+        out = fn()
+    return g, out
+
+
+def per_shape(ops, quant, device, peak):
+    """Each projection alone: one graph of calls over >= 512 MiB of distinct copies (4x L2), replayed 5 times;
+    the median per-call time. A model keeps every layer's weights, so copies stand for the layers in between."""
+    rows = []
+    seen = {}
+    for model, proj, k, n in projections():
+        if (k, n) in seen:
+            rows.append(dict(seen[(k, n)], model=model, proj=proj))
+            continue
+        b = call_bytes(k, n)
+        copies = max(4, -(-(512 << 20) // b))
+        gen = torch.Generator(device=device).manual_seed(k * 31 + n)
+        packed = torch.randint(0, 256, (copies, n, k // 2), dtype=torch.uint8, device=device, generator=gen)
+        scales = (torch.rand(copies, n, k // GROUP, device=device, generator=gen) * 0.01 + 1e-3).half()
+        x = torch.randn(1, k, device=device, generator=gen).half()
+        y = torch.empty(copies, 1, n, dtype=torch.half, device=device)
+        e = ops.ext()
+        st = torch.cuda.current_stream()
+
+        def run():
+            for c in range(copies):   # direct C-ABI calls: no host work inside the graph
+                rc = e.lib.lb_w4_gemv(x.data_ptr(), packed[c].data_ptr(), scales[c].data_ptr(), y[c].data_ptr(), 1,
+                                      n, k, GROUP, 6, 0, torch.cuda.current_stream().cuda_stream)
+                if rc:
+                    raise RuntimeError(e.lib.lb_last_error().decode())
+        g, _ = capture(run)
+        for _ in range(3):
+            g.replay()
+        times = []
+        for _ in range(5):
+            a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            g.replay()
+            bb.record(st)
+            bb.synchronize()
+            times.append(a.elapsed_time(bb) * 1e3 / copies)
+        us = statistics.median(times)
+        row = {"model": model, "proj": proj, "K": k, "N": n, "bytes": b, "us": round(us, 3),
+               "gbs": round(b / (us * 1e-6) / 1e9, 1), "frac": round(b / (us * 1e-6) / 1e9 / peak, 3),
+               "copies": copies}
+        seen[(k, n)] = row
+        rows.append(row)
+        del g, packed, scales, y
+        torch.cuda.empty_cache()
+    return rows
+
+
+def run_ours(args, rank, world, local):
+    from lowbit import ops, quant
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    e = ops.ext()
+    e.set_option("pdl", 1)
+    e.set_option("early_weights", 1)   # the weights are static model state: fetch them before the wait
+    peak, peak_src = measured_peak()
+    projs = projections()
+    step_bytes = sum(call_bytes(k, n) for _, _, k, n in projs)
+    set_bytes = sum(n * k // 2 + 2 * n * (k // GROUP) for _, _, k, n in projs)
+    n_sets = -(-ROTATION_BYTES // set_bytes)
+    sets = build_sets(ops, quant, device, n_sets, seed=1234 + rank)
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    xs = [torch.randn(1, k, device=device, generator=gen).half() for _, _, k, _ in projs]
+
+    # one graph per copy set (21 launches) and one graph over all sets (bulk replay: one host launch per
+    # n_sets steps, so the timed region is never host-bound)
+    def step_fn(layer):
+        return lambda: [ops.linear(x, wq) for x, wq in zip(xs, layer)]
+    set_graphs = [capture(step_fn(layer))[0] for layer in sets]
+    all_graph, _ = capture(lambda: [ops.linear(x, wq) for layer in sets for x, wq in zip(xs, layer)])
+    launches_per_step = len(projs)
+
+    def run_steps(k0, count):
+        i = 0
+        while i < count:
+            if (k0 + i) % n_sets == 0 and count - i >= n_sets:
+                all_graph.replay()
+                i += n_sets
+            else:
+                set_graphs[(k0 + i) % n_sets].replay()
+                i += 1
+
+    st = torch.cuda.current_stream()
+    run_steps(0, args.warmup)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        time.sleep(0.05)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_host0 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(st)
+        run_steps(args.warmup, args.steps)
+        ev1.record(st)
+        ev1.synchronize()
+        torch.cuda.synchronize()
+        t_host1 = time.perf_counter()
+        if dist:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = sampler.summary(t_host0, t_host1)
+    value = world * step_bytes * args.steps / (ms * 1e-3) / 1e9
+    ms_per_step = ms / args.steps
+
+    # e2e: the public API, eager, host buffers in and out every call
+    xs_host = [x.cpu().pin_memory() for x in xs]
+    ys_host = [torch.empty(1, n, dtype=torch.half).pin_memory() for _, _, _, n in projs]
+    h2d = sum(x.numel() * 2 for x in xs_host)
+    d2h = sum(y.numel() * 2 for y in ys_host)
+    e2e_steps = max(3, min(args.steps, 200))
+
+    def e2e_step(layer):
+        for xh, yh, wq in zip(xs_host, ys_host, layer):
+            xd = xh.to(device, non_blocking=True)
+            yh.copy_(ops.linear(xd, wq), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for i in range(3):
+        e2e_step(sets[i % n_sets])
+    if dist:
+        dist.barrier()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(st)
+    for i in range(e2e_steps):
+        e2e_step(sets[i % n_sets])
+    eb.record(st)
+    eb.synchronize()
+    e2e_ms = ea.elapsed_time(eb)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+
+    shapes = None
+    if rank == 0 and not args.no_per_shape:
+        del set_graphs, all_graph
+        sets = None
+        torch.cuda.empty_cache()
+        shapes = per_shape(ops, quant, device, peak)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(budget_s=args.cpu_seconds)
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9 / 1.0
+    traffic = profiled_traffic()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 activations x int4 weights, fp32 accumulate",
+        "data": "synthetic: seeded N(0, 0.02) weights quantized by lowbit's format, N(0, 1) activations",
+        "config": {
+            "workload": "BASELINE config 1: M=1 GEMV over every q/k/v/o/gate/up/down projection of Qwen2.5-0.5B, "
+                        "1.5B and 3B (21 calls per step), group 128, mma layout",
+            "M": 1, "calls_per_step": launches_per_step, "bytes_per_step": step_bytes,
+            "l2": f"cold weights: rotating {n_sets} copy sets = {n_sets * set_bytes / 1e9:.2f} GB "
+                  f"({n_sets * set_bytes / L2_BYTES:.1f}x L2)",
+            "timing": "CUDA graphs (one launch per call, programmatic dependent launch, early weight fetch), "
+                      "CUDA events on the launching stream, max over ranks",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": "gemv_mma_kernel<1,4,2> (M=1 decode GEMV)",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_src,
+            "traffic": traffic,
+            "note": "achieved = algorithmic bytes per launch / average launch duration over the timed region "
+                    "(every launch in the step is this kernel)",
+        },
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps,
+                "how": "lowbit.ops.linear eager per call; pinned-host x -> GPU and y -> pinned host inside the "
+                       "timed region; stream synchronized at the end of each step"},
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if shapes is not None:
+        line["per_shape"] = shapes
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+# ------------------------------------------------------------------------------------------------ CPU arm
+
+def cpu_sweep_inputs(seed=0):
+    """The same workload on the host: the 21 projections, packed canonical weights + scales (CPU tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _, _, k, n in projections():
+        packed = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g)
+        scales = (torch.rand(n, k // GROUP, generator=g) * 0.01 + 1e-3).half()
+        x = torch.randn(1, k, generator=g).half()
+        out.append((x, packed, scales, k, n))
+    return out
+
+
+def cpu_pass(inputs):
+    from oracle import oracle
+    done = 0
+    for x, packed, scales, k, n in inputs:
+        y = oracle.torch_linear(x, packed, scales, GROUP)
+        assert y.shape == (1, n)
+        done += call_bytes(k, n)
+    return done
+
+
+def cpu_baseline(budget_s=10.0):
+    """The reference's CPU path timed on this host's cores: a bounded sample of the workload (whole sweep
+    passes until `budget_s` has elapsed, at least one)."""
+    from oracle import oracle
+    threads = oracle.cpu_threads()
+    torch.set_num_threads(threads)
+    inputs = cpu_sweep_inputs()
+    cpu_pass(inputs[:3])                                     # warm-up (thread pool, allocator)
+    t0 = time.perf_counter()
+    done, passes = 0, 0
+    while passes == 0 or time.perf_counter() - t0 < budget_s:
+        done += cpu_pass(inputs)
+        passes += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{passes} full sweep pass(es) of the 21 projections (M=1) in {dt:.1f} s: "
+                      "oracle.torch_linear = lowbit/ops.py:119-123 dequantize on CPU tensors + fp32 F.linear",
+            "cpu": platform_cpu()}
+
+
+def platform_cpu():
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's own CPU implementation (restated in oracle/, the reference ships no
+    compiled CPU code and has no installable package) on this host's cores, same metric and config."""
+    if rank != 0:
+        return None
+    from oracle import oracle
+    threads = oracle.cpu_threads()
+    torch.set_num_threads(threads)
+    inputs = cpu_sweep_inputs()
+    for _ in range(args.warmup):
+        cpu_pass(inputs)
+    steps = args.steps if args.steps <= 50 else 50
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(steps):
+        done += cpu_pass(inputs)
+    dt = time.perf_counter() - t0
+    val = done / dt / 1e9
+    step_bytes = sum(call_bytes(k, n) for _, _, k, n in projections())
+    return {
+        "impl": "reference",
+        "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantize to fp16, fp32 matmul)",
+        "data": "synthetic: seeded packed weights, N(0, 1) activations",
+        "config": {"workload": "BASELINE config 1 on the host: the 21 Qwen2.5 projections, M=1", "M": 1,
+                   "bytes_per_step": step_bytes, "parallelism": "host cores, rank 0 only"},
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{steps} sweep pass(es); steps capped at 50 to bound the run",
+                         "cpu": platform_cpu()},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30000)
+    ap.add_argument("--warmup", type=int, default=1500)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-per-shape", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local = rank_env()
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,116 @@
+/*
+ * lowbit_b200 -- C ABI of the B200 (sm_100a) W4A16 kernel library.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types. Every entry point validates its arguments
+ * before touching the GPU, launches asynchronously on `stream` (NULL = the legacy default stream) and never
+ * synchronizes. Outputs are caller-allocated. Return value: LB_OK or an lb_status code; lb_last_error()
+ * then holds a message for the calling host thread.
+ *
+ * Weight format (identical bytes to the reference's lowbit/quant.py): a weight W [N, K] is stored as
+ * packed uint8 [N, K/2] (two 4-bit values u = q + 8 per byte, q in [-8, 7]) in one of three layouts --
+ * canonical (lowbit/quant.py:23-35), v3 (lowbit/quant.py:55-64) or mma (lowbit/quant.py:67-78) -- plus
+ * fp16 scales [N, K/G], one per group of G consecutive k (G a multiple of 32, K a multiple of G).
+ * Activations x are fp16 [M, K] row-major, outputs fp16 [M, N] row-major.
+ *
+ * Each entry point replaces one binding of the reference's torch extension (csrc/w4_gemv.cu:542-550) or
+ * one of its host-side helpers; the cited lines are the interface replaced.
+ */
+#ifndef LOWBIT_B200_H
+#define LOWBIT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define LB_API __attribute__((visibility("default")))
+#else
+#define LB_API
+#endif
+
+/* the same handle type as cudaStream_t */
+typedef struct CUstream_st* lb_stream_t;
+
+typedef enum lb_status {
+  LB_OK = 0,
+  LB_ERR_ARGUMENT = 1,    /* sizes, group size, version or row count out of range (TORCH_CHECK in the reference) */
+  LB_ERR_ALIGNMENT = 2,   /* a pointer is not aligned as the kernel's vector loads require */
+  LB_ERR_UNSUPPORTED = 3, /* the current device is not sm_100, or the layout cannot serve this call */
+  LB_ERR_CUDA = 4         /* the CUDA runtime reported an error at launch */
+} lb_status;
+
+typedef enum lb_layout { LB_LAYOUT_CANONICAL = 0, LB_LAYOUT_V3 = 1, LB_LAYOUT_MMA = 2 } lb_layout;
+
+typedef enum lb_option {
+  LB_OPT_PDL = 0,           /* 1 (default): launch with programmatic dependent launch enabled */
+  LB_OPT_EARLY_WEIGHTS = 1, /* 1: GEMV kernels fetch their first weights before waiting on the previous kernel
+                               in the stream (only for weights no in-flight kernel writes); default 0 */
+  LB_OPT_GEMV_KSPLIT = 2,   /* 0 (default): automatic; 1..8 forces the GEMV's K-split cluster size */
+  LB_OPT_GEMV_WARPS = 3     /* 0 (default): automatic; 4 or 8 forces the GEMV's warps per CTA */
+} lb_option;
+
+/* ABI version of this header; bumped on any signature change. */
+#define LB_ABI_VERSION 1
+LB_API int lb_abi_version(void);
+
+LB_API const char* lb_status_string(int status);
+/* message of the last failed call on this host thread ("" after a successful call) */
+LB_API const char* lb_last_error(void);
+
+/* process-wide launch options (lb_option); returns the previous value, or -1 for an unknown option */
+LB_API int lb_set_option(int option, int value);
+LB_API int lb_get_option(int option);
+
+/*
+ * y[M, N] = x[M, K] * dequant(W)^T for 1 <= M <= 8.
+ * Replaces w4_gemv(x, w, s, group, version, rows_per_warp) (csrc/w4_gemv.cu:454-484).
+ *   version 1, 2: w in the canonical layout;  3, 4: the v3 layout;  6: the mma layout (K and group % 128 == 0).
+ *   rows_per_warp: 0 (auto), 1, 2 or 4; used by versions 1-4, accepted and ignored by version 6 (its warps
+ *   always own 16-row tensor-core tiles).
+ * x and w must be 16-byte aligned.
+ */
+LB_API int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+               int64_t group, int version, int rows_per_warp, lb_stream_t stream);
+
+/*
+ * y[M, N] = x[M, K] * dequant(W)^T for 1 <= M <= 64 on the tensor cores, w in the mma layout
+ * (K and group % 128 == 0).
+ * Replaces w4_gemm_tc(x, w, s, group, row_tiles) (csrc/w4_gemv.cu:486-515).
+ *   row_tiles: 0 (auto), 1, 2 or 4 -- accepted for compatibility; the kernel picks its own tiling.
+ */
+LB_API int lb_w4_gemm_tc(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+                  int64_t group, int row_tiles, lb_stream_t stream);
+
+/*
+ * out[N, K] fp16 = fp16_rn((u - 8) * scale), bit-identical to the reference's dequantize kernels.
+ * Replaces w4_dequant(w, s, group, mma_layout) (csrc/w4_gemv.cu:517-540); layout is an lb_layout
+ * (the reference's mma_layout=False/True are LB_LAYOUT_CANONICAL / LB_LAYOUT_MMA).
+ * w and out must be 16-byte aligned.
+ */
+LB_API int lb_w4_dequant(const void* w, const void* scales, void* out, int64_t n, int64_t k, int64_t group, int layout,
+                  lb_stream_t stream);
+
+/*
+ * Quantize W [N, K] (fp32, or fp16 when w_is_half) into canonical packed [N, K/2] + fp16 scales [N, K/G].
+ * With clip_grid == NULL (or n_clip == 0) the bits equal lowbit/quant.py:23-35. With a clip grid
+ * (host array of n_clip <= 32 factors), each group keeps the first factor whose squared error is smallest.
+ * Replaces quantize_w4_gpu(w, group, clip_grid) (lowbit/ops.py:81-116).
+ */
+LB_API int lb_w4_quantize(const void* w, int w_is_half, void* packed, void* scales, int64_t n, int64_t k, int64_t group,
+                   const float* clip_grid, int n_clip, lb_stream_t stream);
+
+/*
+ * Reorder canonical packed bytes [N, K/2] into the v3 (layout 1) or mma (layout 2, K % 128 == 0) layout.
+ * Replaces the host-side quant.interleave_for_gpu / interleave_for_mma calls of W4Weight
+ * (lowbit/ops.py:43-44, lowbit/quant.py:55-78). src and dst must not overlap.
+ */
+LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, int layout, lb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOWBIT_B200_H */

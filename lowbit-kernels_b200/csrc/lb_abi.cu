@@ -1,0 +1,224 @@
+// The C ABI (include/lowbit_b200.h): argument validation with the reference's error contract
+// (csrc/w4_gemv.cu:312-325 and the per-op checks at :454-540), tiling heuristics, kernel launches.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/lowbit_b200.h"
+#include "lb_launch.h"
+
+namespace {
+
+thread_local char g_err[512];
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = 0;
+  return LB_OK;
+}
+
+std::atomic<int> g_opt[4] = {{1}, {0}, {0}, {0}};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
+
+// The library carries sm_100a code only: refuse other devices with a clear message instead of a launch error.
+int check_device() {
+  static thread_local int cached_dev = -1, cached_ok = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(LB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev == cached_dev && cached_ok) return LB_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(LB_ERR_UNSUPPORTED, "lowbit_b200 is built for sm_100a (B200); device %d is sm_%d%d", dev, major, minor);
+  cached_dev = dev;
+  cached_ok = 1;
+  return LB_OK;
+}
+
+int launched(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(LB_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+// csrc/w4_gemv.cu:312-325 for raw pointers: shapes, group size, 16-byte alignment of x and w
+int check_common(const void* x, const void* w, const void* s, const void* y, int64_t m, int64_t n, int64_t k,
+                 int64_t group) {
+  if (!x || !w || !s || !y) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (group <= 0) return fail(LB_ERR_ARGUMENT, "group size must be positive");
+  if (n <= 0 || k <= 0 || m < 0) return fail(LB_ERR_ARGUMENT, "shape mismatch: M=%lld N=%lld K=%lld",
+                                             (long long)m, (long long)n, (long long)k);
+  if (group % 32 || k % group)
+    return fail(LB_ERR_ARGUMENT, "K must be a multiple of the group size, itself a multiple of 32");
+  if (n > (1 << 30) || k > (1 << 28)) return fail(LB_ERR_ARGUMENT, "N or K too large");
+  if (!aligned16(x) || !aligned16(w)) return fail(LB_ERR_ALIGNMENT, "x and w must be 16-byte aligned for the 128-bit loads");
+  if (!aligned2(s) || !aligned2(y)) return fail(LB_ERR_ALIGNMENT, "scales and y must be 2-byte aligned");
+  return LB_OK;
+}
+
+// GEMV tiling: 16-row tiles, NW warps splitting K inside a CTA, a cluster of S CTAs splitting it further.
+// S grows until there are about four CTAs per SM, while every warp keeps at least two 128-wide chunks,
+// and until the staged activations fit comfortably in shared memory.
+lb::GemvConfig gemv_config(int M, int N, int K) {
+  lb::GemvConfig c;
+  c.mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
+  c.warps = 4;
+  c.pdl = g_opt[LB_OPT_PDL].load();
+  const int nt = (N + 15) / 16, kc = K >> 7;
+  const int target = 148 * 4;
+  int s_occ = (target + nt - 1) / nt;
+  int s_chunks = kc / (2 * c.warps);
+  int s = s_occ < s_chunks ? s_occ : s_chunks;
+  if (s < 1) s = 1;
+  while (s < 8 && lb::gemv_mma_smem_bytes(M, K, s, c.mt, c.warps) > 96 * 1024) ++s;
+  if (s > 8) s = 8;
+  int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
+  if (forced >= 1 && forced <= 8) s = forced;
+  if (s > kc) s = kc;
+  int fw = g_opt[LB_OPT_GEMV_WARPS].load();
+  if ((fw == 4 || fw == 8) && c.mt <= 2) c.warps = fw;
+  c.ksplit = s;
+  return c;
+}
+
+int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
+                 int64_t group, cudaStream_t st) {
+  lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0};
+  lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
+  if (lb::gemv_mma_smem_bytes((int)m, (int)k, c.ksplit, c.mt, c.warps) > 227 * 1024)
+    return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
+  return launched(lb::launch_gemv_mma(p, c, st), "w4_gemv");
+}
+
+}  // namespace
+
+extern "C" {
+
+int lb_abi_version(void) { return LB_ABI_VERSION; }
+
+const char* lb_status_string(int status) {
+  switch (status) {
+    case LB_OK: return "ok";
+    case LB_ERR_ARGUMENT: return "invalid argument";
+    case LB_ERR_ALIGNMENT: return "misaligned pointer";
+    case LB_ERR_UNSUPPORTED: return "unsupported device or layout";
+    case LB_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* lb_last_error(void) { return g_err; }
+
+int lb_set_option(int option, int value) {
+  if (option < 0 || option > 3) return -1;
+  return g_opt[option].exchange(value);
+}
+
+int lb_get_option(int option) {
+  if (option < 0 || option > 3) return -1;
+  return g_opt[option].load();
+}
+
+int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+               int64_t group, int version, int rows_per_warp, lb_stream_t stream) {
+  int rc = check_common(x, w, scales, y, m, n, k, group);
+  if (rc) return rc;
+  if (m < 1 || m > 8)
+    return fail(LB_ERR_ARGUMENT, "the GEMV kernels take 1..8 rows; use the dequantize + matmul path above that");
+  if (!((version >= 1 && version <= 4) || version == 6)) return fail(LB_ERR_ARGUMENT, "version is 1..4 or 6");
+  if (version == 6 && (k % 128 || group % 128))
+    return fail(LB_ERR_ARGUMENT, "v6 needs K and the group size to be multiples of 128");
+  if (!(rows_per_warp == 0 || rows_per_warp == 1 || rows_per_warp == 2 || rows_per_warp == 4))
+    return fail(LB_ERR_ARGUMENT, "rows_per_warp is 0 (auto), 1, 2 or 4");
+  if ((rc = check_device())) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (version == 6) return run_gemv_mma(x, w, scales, y, m, n, k, group, st);
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group, 0};
+  int R = rows_per_warp ? rows_per_warp : (n >= 512 ? 4 : (m >= 4 ? 2 : 1));
+  return launched(lb::launch_gemv_compat(p, R, version >= 3, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemv");
+}
+
+int lb_w4_gemm_tc(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+                  int64_t group, int row_tiles, lb_stream_t stream) {
+  int rc = check_common(x, w, scales, y, m, n, k, group);
+  if (rc) return rc;
+  if (m < 1 || m > 64) return fail(LB_ERR_ARGUMENT, "the tensor-core kernel takes 1..64 rows");
+  if (k % 128 || group % 128) return fail(LB_ERR_ARGUMENT, "v5 needs K and the group size to be multiples of 128");
+  if (!(row_tiles == 0 || row_tiles == 1 || row_tiles == 2 || row_tiles == 4))
+    return fail(LB_ERR_ARGUMENT, "row_tiles must be 1, 2 or 4");
+  if ((rc = check_device())) return rc;
+  return run_gemv_mma(x, w, scales, y, m, n, k, group, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lb_w4_dequant(const void* w, const void* scales, void* out, int64_t n, int64_t k, int64_t group, int layout,
+                  lb_stream_t stream) {
+  if (!w || !scales || !out) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (group <= 0) return fail(LB_ERR_ARGUMENT, "w [N,K/2], scales [N,K/G], positive group size");
+  if (n <= 0 || k <= 0 || group % 32 || k % group) return fail(LB_ERR_ARGUMENT, "shape mismatch");
+  if (n > (1 << 30) || k > (1 << 28)) return fail(LB_ERR_ARGUMENT, "N or K too large");
+  if (layout < 0 || layout > 2) return fail(LB_ERR_ARGUMENT, "layout is 0 (canonical), 1 (v3) or 2 (mma)");
+  if (layout == 2 && (k % 128 || group % 128))
+    return fail(LB_ERR_ARGUMENT, "the v5 layout needs K and group % 128 == 0");
+  if (!aligned16(w) || !aligned16(out))
+    return fail(LB_ERR_ALIGNMENT, "packed weights must be contiguous and 16-byte aligned");
+  if (!aligned2(scales)) return fail(LB_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_dequant(w, scales, reinterpret_cast<__half*>(out), (int)n, (int)k, (int)group, layout,
+                                     reinterpret_cast<cudaStream_t>(stream)),
+                  "w4_dequant");
+}
+
+int lb_w4_quantize(const void* w, int w_is_half, void* packed, void* scales, int64_t n, int64_t k, int64_t group,
+                   const float* clip_grid, int n_clip, lb_stream_t stream) {
+  if (!w || !packed || !scales) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (group <= 0 || n <= 0 || k <= 0 || k % group || group % 32)
+    return fail(LB_ERR_ARGUMENT, "K=%lld must be a multiple of the group size %lld, itself a multiple of 32",
+                (long long)k, (long long)group);
+  if (n > (1 << 30) || k > (1 << 28)) return fail(LB_ERR_ARGUMENT, "N or K too large");
+  if (n_clip < 0 || n_clip > 32 || (n_clip > 0 && !clip_grid))
+    return fail(LB_ERR_ARGUMENT, "clip grid holds 0..32 factors");
+  for (int i = 0; i < n_clip; ++i)
+    if (!(clip_grid[i] > 0.f)) return fail(LB_ERR_ARGUMENT, "clip factors must be positive");
+  if (!aligned2(scales) || (w_is_half ? !aligned2(w) : (reinterpret_cast<uintptr_t>(w) & 3u) != 0))
+    return fail(LB_ERR_ALIGNMENT, "misaligned weight or scale pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_quantize(w, w_is_half, reinterpret_cast<uint8_t*>(packed),
+                                      reinterpret_cast<__half*>(scales), (int)n, (int)k, (int)group, clip_grid,
+                                      n_clip, reinterpret_cast<cudaStream_t>(stream)),
+                  "w4_quantize");
+}
+
+int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, int layout, lb_stream_t stream) {
+  if (!canonical || !dst) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (n <= 0 || k <= 0 || k % 8) return fail(LB_ERR_ARGUMENT, "K must be a positive multiple of 8");
+  if (n > (1 << 30) || k > (1 << 28)) return fail(LB_ERR_ARGUMENT, "N or K too large");
+  if (layout != 1 && layout != 2) return fail(LB_ERR_ARGUMENT, "repack layout is 1 (v3) or 2 (mma)");
+  if (layout == 2 && k % 128)
+    return fail(LB_ERR_ARGUMENT, "K=%lld must be a multiple of 128 for the tensor-core layout", (long long)k);
+  if ((reinterpret_cast<uintptr_t>(dst) & 3u) != 0) return fail(LB_ERR_ALIGNMENT, "dst must be 4-byte aligned");
+  const char* a = static_cast<const char*>(canonical);
+  const char* b = static_cast<const char*>(dst);
+  const size_t bytes = (size_t)n * (size_t)(k / 2);
+  if (a < b + bytes && b < a + bytes) return fail(LB_ERR_ARGUMENT, "src and dst overlap");
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_repack(static_cast<const uint8_t*>(canonical), static_cast<uint8_t*>(dst), (int)n,
+                                    (int)k, layout, reinterpret_cast<cudaStream_t>(stream)),
+                  "w4_repack");
+}
+
+}  // extern "C"

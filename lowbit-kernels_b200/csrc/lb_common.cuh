@@ -1,0 +1,87 @@
+// Shared device helpers for the W4A16 kernels (sm_100a).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lb {
+
+// fp16 constants as packed f16x2 bit patterns
+constexpr uint32_t kMagic = 0x64006400u;     // 1024.0 | 1024.0: OR-ing a nibble u into the mantissa gives 1024 + u
+constexpr uint32_t kBias1032 = 0x64086408u;  // 1032.0 = 1024 + 8
+constexpr uint32_t kSixteenth = 0x2C002C00u; // 1 / 16
+constexpr uint32_t kMinus72 = 0xD480D480u;   // -72.0 = -(1024 / 16 + 8)
+
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Signed values of nibble pair j = 0 and j = 1 of a word in the v3 slot order, as exact f16x2.
+//   pair 0: slots 0 and 4 (bits 0-3, 16-19)      -> (1024 + u) - 1032
+//   pair 1: slots 1 and 5 (bits 4-7, 20-23)      -> (1024 + 16u) / 16 - 72
+// Both results are small integers, so every step is exact. Pairs 2 and 3 are the same on (word >> 8).
+__device__ __forceinline__ uint32_t q_pair_lo(uint32_t word) {
+  return hsub2_bits((word & 0x000F000Fu) | kMagic, kBias1032);
+}
+__device__ __forceinline__ uint32_t q_pair_hi(uint32_t word) {
+  return hfma2_bits((word & 0x00F000F0u) | kMagic, kSixteenth, kMinus72);
+}
+
+// Pair j (0..3) of a v3-order word as exact f16x2 of (u - 8): (k0 + 2j, k0 + 2j + 1)
+__device__ __forceinline__ uint32_t q_pair(uint32_t word, int j) {
+  return hsub2_bits(((word >> (4 * j)) & 0x000F000Fu) | kMagic, kBias1032);
+}
+
+// Streaming 128-bit load of data read exactly once (weights): no L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Programmatic dependent launch: let the next kernel in the stream launch, and wait for the previous one.
+// Both are no-ops when the launch carries no programmatic dependency.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// D += A * B, m16n8k16, f16 inputs, f32 accumulators (PTX ISA fragment layout: lane = 4g + t;
+// a0 = A[g][2t..2t+1], a1 = A[g+8][2t..], a2 = A[g][2t+8..], a3 = A[g+8][2t+8..]; b0 = B[2t..][g], b1 = B[2t+8..][g];
+// d0,d1 = D[g][2t, 2t+1], d2,d3 = D[g+8][2t, 2t+1]).
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace lb

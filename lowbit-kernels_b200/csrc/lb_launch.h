@@ -1,0 +1,49 @@
+// Host-side launch descriptors shared by the C-ABI layer and the kernel files.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace lb {
+
+enum : int {
+  kFlagEarlyWeights = 1,  // issue the first weight loads before waiting on the predecessor kernel
+};
+
+struct GemvParams {
+  const void* x;  // fp16 [M, K]
+  const void* w;  // packed uint8 [N, K / 2]
+  const void* s;  // fp16 [N, K / G]
+  __half* y;      // fp16 [M, N]
+  int M, N, K, G;
+  int flags;
+};
+
+struct GemvConfig {
+  int mt;      // n8 activation tiles (1: M <= 8, 2: M <= 16)
+  int warps;   // warps per CTA (4 or 8)
+  int ksplit;  // CTAs per cluster splitting K (1..8)
+  int pdl;     // launch with programmatic stream serialization
+};
+
+cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
+size_t gemv_mma_smem_bytes(int M, int K, int nsplit, int mt, int nw);
+cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
+
+// format kernels (lb_format.cu)
+cudaError_t launch_dequant(const void* w, const void* s, __half* out, int N, int K, int G, int layout,
+                           cudaStream_t st);
+cudaError_t launch_quantize(const void* w, int w_is_half, uint8_t* packed, __half* scales, int N, int K, int G,
+                            const float* clip, int n_clip, cudaStream_t st);
+cudaError_t launch_repack(const uint8_t* canonical, uint8_t* out, int N, int K, int layout, cudaStream_t st);
+
+// tensor-core skinny GEMM (lb_gemm_tc.cu)
+struct GemmConfig {
+  int n_tile;   // MMA N (activation rows, padded): 16, 32, 48 or 64
+  int ksplit;   // CTAs per cluster splitting K
+  int pdl;
+};
+cudaError_t launch_gemm_tc(const GemvParams& p, const GemmConfig& c, cudaStream_t st);
+
+}  // namespace lb

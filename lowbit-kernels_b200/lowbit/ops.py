@@ -1,0 +1,208 @@
+"""Operator API of the B200 W4A16 library: weights on the GPU, decode GEMV / skinny GEMM, prefill dequantize.
+
+Drop-in for lowbit/ops.py of YuchenHe985/lowbit-kernels: the same public names, arguments, defaults and
+exceptions. What differs is underneath: the kernels are hand-written for sm_100a and reached through a C ABI
+(include/lowbit_b200.h, loaded by ``ext()``), layouts are built on the GPU, and the row-count dispatch
+constants come from a B200 sweep (dispatch_b200.json).
+
+Kernel versions (``gemv(x, wq, version)``; the reference's numbering, csrc/w4_gemv.cu:1-22):
+  1, 2  canonical layout, M <= 8        -- compatibility kernels (fp32 accumulation)
+  3, 4  v3 layout, M <= 8               -- compatibility kernels (fp32 accumulation)
+  6     mma layout, M <= 8              -- the decode GEMV (tensor-core fragments fed from registers)
+  5     mma layout, M <= 64             -- the skinny tensor-core GEMM
+"""
+import json
+import os
+import pathlib
+
+import torch
+
+from . import quant
+from ._lib import Ext
+
+_EXT = None
+
+
+def ext():
+    """The kernel library (built ahead of time by build.py; no JIT, no fallback). Raises if it cannot load."""
+    global _EXT
+    if _EXT is None:
+        _EXT = Ext()
+    return _EXT
+
+
+LAYOUTS = ("canonical", "v3", "mma")
+
+
+def _to_device_u8(a, device):
+    t = a if isinstance(a, torch.Tensor) else torch.from_numpy(a)
+    return t.to(device=device, dtype=torch.uint8).contiguous()
+
+
+def _to_device_f16(a, device):
+    t = a if isinstance(a, torch.Tensor) else torch.from_numpy(a)
+    return t.to(device=device, dtype=torch.float16).contiguous()
+
+
+class W4Weight:
+    """One linear layer's weight in the lowbit/quant.py format, on the GPU. `layouts` picks which copies to keep:
+    canonical (versions 1, 2, dequantize), v3 (3, 4), mma (5, 6, dequantize; K and the group size multiples of
+    128). None = every layout this shape supports; a model keeps ("mma",). Prefill dequantizes, so one of
+    canonical / mma must be kept. `packed` is the canonical layout as a numpy array or a torch tensor (host or
+    GPU); the other layouts are built from it on the GPU (lowbit/ops.py:24-54)."""
+
+    def __init__(self, packed, scales, group, layouts=None, device=None):
+        self.group = group
+        self.n, self.k = int(packed.shape[0]), int(packed.shape[1]) * 2
+        mma_ok = self.k % 128 == 0 and group % 128 == 0
+        if layouts is None:
+            layouts = LAYOUTS if mma_ok else ("canonical", "v3")
+        if not set(layouts) <= set(LAYOUTS):
+            raise ValueError(f"unknown layout in {layouts}; choose from {LAYOUTS}")
+        if "mma" in layouts and not mma_ok:
+            raise ValueError(f"the mma layout needs K and the group size to be multiples of 128 (K={self.k}, G={group})")
+        if "canonical" not in layouts and "mma" not in layouts:
+            raise ValueError("keep the canonical or the mma layout: prefill dequantizes from one of them")
+        if device is None:
+            device = packed.device if isinstance(packed, torch.Tensor) and packed.is_cuda else torch.device("cuda")
+        canonical = _to_device_u8(packed, device)
+        self.scales = _to_device_f16(scales, device)
+        self.packed_v3 = ext().w4_repack(canonical, "v3") if "v3" in layouts else None
+        self.packed_mma = ext().w4_repack(canonical, "mma") if "mma" in layouts else None
+        self.packed = canonical if "canonical" in layouts else None
+
+    @classmethod
+    def from_float(cls, w, group=128, layouts=None):
+        """Quantize a float weight [N, K] (on the GPU, bit-identical to quant.quantize_w4) and keep `layouts`."""
+        packed, scales = quantize_w4_gpu(w, group)
+        return cls(packed, scales, group, layouts)
+
+    def nbytes(self):
+        """Bytes of one copy of the weight (packed values + scales), whatever layouts are kept."""
+        return self.n * self.k // 2 + self.scales.numel() * 2
+
+
+def pick_rows(n, m):
+    """Rows per warp the compatibility kernels (versions 1-4) use when rows_per_warp = 0 (csrc/w4_gemv.cu:424-427)."""
+    return 4 if n >= 512 else 2 if m >= 4 else 1
+
+
+# the layout each kernel version reads, and the most rows it takes
+NEEDS = {1: "packed", 2: "packed", 3: "packed_v3", 4: "packed_v3", 5: "packed_mma", 6: "packed_mma"}
+MAX_ROWS = {1: 8, 2: 8, 3: 8, 4: 8, 5: 64, 6: 8}
+
+
+def gemv(x, wq, version=4, rows_per_warp=0):
+    """x [M, K] fp16 -> [M, N] fp16. Versions 1-4 and 6: M <= 8; version 5: M <= 64 (tensor cores).
+    Versions 5 and 6 read the same layout (packed_mma), so a model needs only that copy."""
+    if version not in NEEDS:
+        raise ValueError(f"version must be one of {sorted(NEEDS)}")
+    if getattr(wq, NEEDS[version]) is None:
+        raise ValueError(f"v{version} reads {NEEDS[version]}, which this W4Weight does not keep")
+    if version == 5:
+        return ext().w4_gemm_tc(x.contiguous(), wq.packed_mma, wq.scales, wq.group, rows_per_warp)
+    w = wq.packed_mma if version == 6 else wq.packed_v3 if version >= 3 else wq.packed
+    return ext().w4_gemv(x.contiguous(), w, wq.scales, wq.group, version, rows_per_warp)
+
+
+def quantize_w4_gpu(w, group=128, clip_grid=None, rows_per_pass=2048):
+    """Same format and, with clip_grid=None, the same bits as quant.quantize_w4, computed by the quantize kernel.
+    clip_grid, e.g. (1.0, 0.95, ..., 0.75): per group, try scale = a * amax / 7 for each a and keep the first one
+    with the smallest squared weight error. Returns (packed uint8 [N, K/2], scales fp16 [N, K/G]) on the GPU.
+    Rows are converted and quantized `rows_per_pass` at a time, which bounds the fp32 staging copy
+    (lowbit/ops.py:81-116)."""
+    n, k = w.shape
+    if group <= 0 or k % group or group % 32:
+        raise ValueError(f"K={k} must be a multiple of the group size {group}, itself a multiple of 32")
+    if clip_grid is not None and len(clip_grid) > 32:
+        raise ValueError("clip_grid holds at most 32 factors")
+    dev = w.device if isinstance(w, torch.Tensor) and w.is_cuda else torch.device("cuda")
+    if not isinstance(w, torch.Tensor):
+        w = torch.as_tensor(w)
+    packed = torch.empty(n, k // 2, dtype=torch.uint8, device=dev)
+    scales = torch.empty(n, k // group, dtype=torch.float16, device=dev)
+    for r0 in range(0, n, rows_per_pass):
+        part = w[r0:r0 + rows_per_pass].detach()
+        if part.dtype not in (torch.float32, torch.float16):
+            part = part.float()
+        p, s = ext().w4_quantize(part.to(dev).contiguous(), group, clip_grid)
+        packed[r0:r0 + rows_per_pass] = p
+        scales[r0:r0 + rows_per_pass] = s
+    return packed, scales
+
+
+def dequantize_w4_gpu(packed, scales, group=128):
+    """fp16 [N, K] from canonical packed weights on the GPU: (u - 8) * scale rounded once to fp16, the bits the
+    reference's lowbit/ops.py:119-123 gives. Host arrays belong to quant.dequantize_w4."""
+    if not (isinstance(packed, torch.Tensor) and packed.is_cuda):
+        raise RuntimeError("dequantize_w4_gpu takes GPU tensors; use lowbit.quant.dequantize_w4 for host arrays")
+    return ext().w4_dequant(packed.contiguous(), scales.contiguous(), group, layout="canonical")
+
+
+def dequant(wq, layout=None):
+    """fp16 W [N, K] from the canonical or the mma copy (None: canonical when kept). Both give the same bits."""
+    if layout is None:
+        layout = "canonical" if wq.packed is not None else "mma"
+    if layout == "canonical" and wq.packed is not None:
+        return ext().w4_dequant(wq.packed, wq.scales, wq.group)
+    if layout == "mma" and wq.packed_mma is not None:
+        return ext().w4_dequant(wq.packed_mma, wq.scales, wq.group, True)
+    raise ValueError(f"cannot dequantize from the {layout} layout: not kept")
+
+
+# ------------------------------------------------------------------------------------------ dispatch constants
+#
+# linear() picks, by row count and layer width: version 6 for up to AUTO_GEMV_ROWS rows, version 5 up to
+# AUTO_V5_ROWS rows (AUTO_V5_WIDE_ROWS on layers with N >= AUTO_WIDE_N), dequantize + cuBLAS above. The values
+# come from dispatch_b200.json (a B200 sweep). LOWBIT_DISPATCH=reference restores the reference's T4 values
+# (lowbit/ops.py:142), under which the reference's own dispatch tests hold verbatim.
+
+_REFERENCE_TABLE = {"AUTO_GEMV_ROWS": 1, "AUTO_V5_ROWS": 32, "AUTO_V5_WIDE_ROWS": 64, "AUTO_WIDE_N": 3072}
+DISPATCH_TABLE_PATH = pathlib.Path(__file__).resolve().parent / "dispatch_b200.json"
+
+
+def _load_dispatch():
+    if os.environ.get("LOWBIT_DISPATCH", "") == "reference":
+        return dict(_REFERENCE_TABLE, source="reference T4 constants (lowbit/ops.py:142)")
+    table = json.loads(DISPATCH_TABLE_PATH.read_text())
+    return table
+
+
+DISPATCH = _load_dispatch()
+AUTO_GEMV_ROWS, AUTO_V5_ROWS, AUTO_V5_WIDE_ROWS, AUTO_WIDE_N = (
+    int(DISPATCH[k]) for k in ("AUTO_GEMV_ROWS", "AUTO_V5_ROWS", "AUTO_V5_WIDE_ROWS", "AUTO_WIDE_N"))
+
+
+def gemm_chunked(x, wq, chunk=64):
+    """Many rows through version 5 in 64-row slices (no fp16 weight copy is written)."""
+    return torch.cat([gemv(x[i:i + chunk], wq, 5) for i in range(0, x.shape[0], chunk)])
+
+
+def auto_version(m, wq):
+    """The kernel linear() uses for m rows, or None for dequantize + cuBLAS. Weights without the mma layout use
+    version 4 / 2 up to 8 rows (lowbit/ops.py:151-160)."""
+    if wq.packed_mma is not None:
+        if m <= AUTO_GEMV_ROWS:
+            return 6
+        return 5 if m <= (AUTO_V5_WIDE_ROWS if wq.n >= AUTO_WIDE_N else AUTO_V5_ROWS) else None
+    if m <= 8:
+        return 4 if wq.packed_v3 is not None else 2 if wq.packed is not None else None
+    return None
+
+
+def linear(x, wq, max_gemv_rows=8, version=0):
+    """Decode (few rows): an INT4 kernel; prefill (many rows): dequantize, then cuBLAS fp16 GEMM. version 0 =
+    auto_version; a fixed version runs up to min(max_gemv_rows, its row limit) rows (version 5: 64), and
+    dequantize + cuBLAS above that (lowbit/ops.py:163-178)."""
+    m = x.shape[0]
+    if m == 0:
+        return x.new_empty(0, wq.n)
+    if version == 0:
+        v = auto_version(m, wq)
+    elif version in MAX_ROWS:
+        v = version if m <= (MAX_ROWS[5] if version == 5 else min(max_gemv_rows, MAX_ROWS[version])) else None
+    else:
+        raise ValueError(f"version must be 0 (auto) or one of {sorted(MAX_ROWS)}")
+    if v is not None:
+        return gemv(x, wq, v)
+    return torch.nn.functional.linear(x, dequant(wq, "mma" if wq.packed_mma is not None else "canonical"))
