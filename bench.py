@@ -476,6 +476,20 @@ def run_reference(args, rank, world):
     }
 
 
+def profile_case(k, n, m, copies=8, calls=6):
+    """A handful of cold calls of one shape (8 distinct weight copies, each > L2 / 8 for the large layers) for
+    `ncu -k regex:gemv -s 2 -c 3`: small enough that a --set full capture ends in about a minute."""
+    from lowbit import ops
+    torch.cuda.set_device(0)
+    ops.ext().set_option("early_weights", 1)
+    wqs = [ops.W4Weight.from_float(torch.randn(n, k, device="cuda") * 0.02, GROUP, ("mma",)) for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda").half()
+    for i in range(calls):
+        ops.linear(x, wqs[i % copies])
+    torch.cuda.synchronize()
+    print(f"profile case K={k} N={n} M={m}: {calls} calls done", file=sys.stderr)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -485,7 +499,12 @@ def main():
     ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-case", default=None, metavar="K,N,M",
+                    help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(*(int(v) for v in args.profile_case.split(",")))
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local = rank_env()

@@ -49,30 +49,35 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(GemvParams p) {
 
   pdl_launch_dependents();
 
-  // this warp's chunks: c_begin + warp + NW * i
-  const int first = c_begin + warp;
-  uint4 qa[U], qb[U];
-  uint16_t sca[U], scb[U];
-  auto load = [&](int c0) {
+  // This warp's chunks are c_begin + warp + NW * i. Two register buffers of U chunks each alternate: the
+  // loads of one are in flight while the other is consumed, and a buffer is refilled right after use, so
+  // a warp never waits for one batch before requesting the next.
+  const int first = c_begin + warp, stride = NW * U;
+  uint4 a0[U], b0[U], a1[U], b1[U];      // buffer 0 / 1: rows g (a) and g + 8 (b)
+  uint16_t sa0[U], sb0[U], sa1[U], sb1[U];
+  auto load = [&](uint4 (&qa)[U], uint4 (&qb)[U], uint16_t (&ssa)[U], uint16_t (&ssb)[U], int c0) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      int c = c0 + NW * u;
+      const int c = c0 + NW * u;
       if (c < c_end) {
-        int grp = cpg == 1 ? c : c / cpg;
+        const int grp = cpg == 1 ? c : c / cpg;
         qa[u] = ldg_stream(wa + 4 * c);
         qb[u] = ldg_stream(wb + 4 * c);
-        sca[u] = ldg_u16(sa + grp);
-        scb[u] = ldg_u16(sb + grp);
+        ssa[u] = ldg_u16(sa + grp);
+        ssb[u] = ldg_u16(sb + grp);
       }
     }
   };
 
   if (p.flags & kFlagEarlyWeights) {
-    load(first);   // weights and scales are static model state: fetch before the predecessor finishes
+    // weights and scales are static model state: fetch them before the predecessor kernel finishes
+    load(a0, b0, sa0, sb0, first);
+    load(a1, b1, sa1, sb1, first + stride);
     pdl_wait();
   } else {
     pdl_wait();
-    load(first);
+    load(a0, b0, sa0, sb0, first);
+    load(a1, b1, sa1, sb1, first + stride);
   }
 
   // stage x[:, chunks c_begin..c_end) in consumption order: word ((m * row_words) + lc * 64 + qd * 16 + t * 4 + e)
@@ -99,49 +104,53 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(GemvParams p) {
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
 
-  for (int c0 = first; c0 < c_end; c0 += NW * U) {
-    uint4 ca[U], cb[U];
-    uint16_t csa[U], csb[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) { ca[u] = qa[u]; cb[u] = qb[u]; csa[u] = sca[u]; csb[u] = scb[u]; }
-    load(c0 + NW * U);   // prefetch the next batch while this one is computed
+  auto compute = [&](const uint4 (&qa)[U], const uint4 (&qb)[U], const uint16_t (&ssa)[U],
+                     const uint16_t (&ssb)[U], int c0) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      int c = c0 + NW * u;
-      if (c >= c_end) break;
-      const int lc = c - c_begin;
-      float d[MT][4];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d[mt][i] = 0.f;
-#pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
-        uint32_t w0 = (&ca[u].x)[qd], w1 = (&cb[u].x)[qd];
-        uint4 xb[MT];
+      const int c = c0 + NW * u;
+      if (c < c_end) {
+        const int lc = c - c_begin;
+        float d[MT][4];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
-          xb[mt] = *reinterpret_cast<const uint4*>(smem + xoff[mt] + lc * 64 + qd * 16);
-        // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
-        uint32_t a0 = q_pair_lo(w0), a1 = q_pair_lo(w1), a2 = q_pair_hi(w0), a3 = q_pair_hi(w1);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], a0, a1, a2, a3, xb[mt].x, xb[mt].y);
-        // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
-        w0 >>= 8;
-        w1 >>= 8;
-        a0 = q_pair_lo(w0); a1 = q_pair_lo(w1); a2 = q_pair_hi(w0); a3 = q_pair_hi(w1);
+          for (int i = 0; i < 4; ++i) d[mt][i] = 0.f;
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], a0, a1, a2, a3, xb[mt].z, xb[mt].w);
-      }
-      const float s0 = h2f_bits(csa[u]), s1 = h2f_bits(csb[u]);
+        for (int qd = 0; qd < 4; ++qd) {
+          uint32_t w0 = (&qa[u].x)[qd], w1 = (&qb[u].x)[qd];
+          uint4 xb[MT];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
-        acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
-        acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
-        acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+          for (int mt = 0; mt < MT; ++mt)
+            xb[mt] = *reinterpret_cast<const uint4*>(smem + xoff[mt] + lc * 64 + qd * 16);
+          // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
+          uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
+          // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
+          w0 >>= 8;
+          w1 >>= 8;
+          f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+        }
+        const float s0 = h2f_bits(ssa[u]), s1 = h2f_bits(ssb[u]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
+          acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
+          acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
+          acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+        }
       }
     }
+  };
+
+  for (int c0 = first; c0 < c_end; c0 += 2 * stride) {
+    compute(a0, b0, sa0, sb0, c0);
+    load(a0, b0, sa0, sb0, c0 + 2 * stride);
+    compute(a1, b1, sa1, sb1, c0 + stride);
+    load(a1, b1, sa1, sb1, c0 + 3 * stride);
   }
 
   // reduce the NW warps' partial tiles: red[warp][mt][i][lane]
@@ -153,37 +162,40 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(GemvParams p) {
     for (int i = 0; i < 4; ++i) red[((warp * MT + mt) * 4 + i) * 32 + lane] = acc[mt][i];
   __syncthreads();
 
-  // thread e (< MT * 128) owns element e of the tile: (mt, i, lane)
-  const int tile_elems = MT * 128;
-  float v = 0.f;
-  const int e = threadIdx.x;
-  if (e < tile_elems) {
+  // element e of the tile is (mt = e / 128, i = e / 32 % 4, lane = e % 32); a CTA has fewer threads than
+  // a multi-tile (MT > 1) tile has elements, so threads stride over them
+  constexpr int kTile = MT * 128;
+  auto store = [&](int e, float v) {
+    const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+    const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+    const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
+    if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+  };
+  auto cta_sum = [&](int e) {
+    float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) v += red[w * tile_elems + e];
-  }
+    for (int w = 0; w < NW; ++w) v += red[w * kTile + e];
+    return v;
+  };
 
   if (nsplit > 1) {
     // cluster split-K: every CTA writes its partial tile into its slot of rank 0's buffer; rank 0 sums the
     // slots in rank order. The first cluster barrier makes sure rank 0 is past its main loop (the buffer
     // overlaps its activation stage), the second that every slot has landed.
     cg::cluster_group cluster = cg::this_cluster();
-    float* part = red + NW * tile_elems;  // [nsplit][tile_elems] in rank 0's shared memory
+    float* part = red + NW * kTile;  // [nsplit][kTile] in rank 0's shared memory
     float* dst = cluster.map_shared_rank(part, 0);
     cluster.sync();
-    if (e < tile_elems) dst[split * tile_elems + e] = v;
+    for (int e = threadIdx.x; e < kTile; e += NW * 32) dst[split * kTile + e] = cta_sum(e);
     cluster.sync();
     if (split != 0) return;
-    if (e < tile_elems) {
-      v = 0.f;
-      for (int r = 0; r < nsplit; ++r) v += part[r * tile_elems + e];
+    for (int e = threadIdx.x; e < kTile; e += NW * 32) {
+      float v = 0.f;
+      for (int r = 0; r < nsplit; ++r) v += part[r * kTile + e];
+      store(e, v);
     }
-  }
-
-  if (e < tile_elems) {
-    const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-    const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-    const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-    if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+  } else {
+    for (int e = threadIdx.x; e < kTile; e += NW * 32) store(e, cta_sum(e));
   }
 }
 
