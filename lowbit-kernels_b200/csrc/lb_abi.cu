@@ -27,6 +27,8 @@ int ok() {
 
 std::atomic<int> g_opt[4] = {{1}, {0}, {0}, {0}};
 
+int g_sm_count = 0;  // SMs of the current device (set by check_device)
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
 
@@ -42,6 +44,7 @@ int check_device() {
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   if (major != 10 || minor != 0)
     return fail(LB_ERR_UNSUPPORTED, "lowbit_b200 is built for sm_100a (B200); device %d is sm_%d%d", dev, major, minor);
+  cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
   cached_dev = dev;
   cached_ok = 1;
   return LB_OK;
@@ -67,29 +70,45 @@ int check_common(const void* x, const void* w, const void* s, const void* y, int
   return LB_OK;
 }
 
-// GEMV tiling: 16-row tiles, NW warps splitting K inside a CTA, a cluster of S CTAs splitting it further.
-// S grows until there are about four CTAs per SM, while every warp keeps at least two 128-wide chunks,
-// and until the staged activations fit comfortably in shared memory.
+// GEMV tiling. Persistent CTAs walk 16-row tiles; the warps of a CTA split each tile's 128-wide chunks; a
+// cluster of S CTAs splits K further. A configuration is (warps NW, split S); CTAs per SM follow from NW
+// (16 resident warps per SM) and shared memory. The model: an SM's time is the bytes its busiest CTA slot
+// streams -- ceil(tiles / clusters) tiles of nl = ceil(KC / S) chunks -- times the CTAs sharing the SM,
+// with idle warps (nl not a multiple of NW) counted as if busy and a small charge per cluster split.
 lb::GemvConfig gemv_config(int M, int N, int K) {
-  lb::GemvConfig c;
-  c.mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
-  c.warps = 4;
-  c.pdl = g_opt[LB_OPT_PDL].load();
+  lb::GemvConfig best{};
+  best.mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
+  best.pdl = g_opt[LB_OPT_PDL].load();
+  const int sms = g_sm_count > 0 ? g_sm_count : 148;
   const int nt = (N + 15) / 16, kc = K >> 7;
-  const int target = 148 * 4;
-  int s_occ = (target + nt - 1) / nt;
-  int s_chunks = kc / (2 * c.warps);
-  int s = s_occ < s_chunks ? s_occ : s_chunks;
-  if (s < 1) s = 1;
-  while (s < 8 && lb::gemv_mma_smem_bytes(M, K, s, c.mt, c.warps) > 96 * 1024) ++s;
-  if (s > 8) s = 8;
-  int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
-  if (forced >= 1 && forced <= 8) s = forced;
-  if (s > kc) s = kc;
-  int fw = g_opt[LB_OPT_GEMV_WARPS].load();
-  if ((fw == 4 || fw == 8) && c.mt <= 2) c.warps = fw;
-  c.ksplit = s;
-  return c;
+  const int forced_s = g_opt[LB_OPT_GEMV_KSPLIT].load(), forced_w = g_opt[LB_OPT_GEMV_WARPS].load();
+  double best_cost = 1e30;
+  for (int nw : {16, 8, 4}) {
+    if (best.mt >= 4 && nw == 16) continue;
+    if (forced_w && nw != forced_w) continue;
+    for (int s = 1; s <= 8 && s <= kc; ++s) {
+      if (forced_s && s != forced_s) continue;
+      const size_t smem = lb::gemv_smem_bytes(M, K, s, best.mt, nw);
+      if (smem > 227 * 1024) continue;
+      int per_sm = 16 / nw;
+      while (per_sm > 1 && (size_t)per_sm * smem > 220 * 1024) --per_sm;
+      int clusters = sms * per_sm / s;
+      if (clusters > nt) clusters = nt;
+      if (clusters < 1) clusters = 1;
+      const int nl = (kc + s - 1) / s;
+      const int cpw = (nl + nw - 1) / nw;
+      const double tiles_per = (double)((nt + clusters - 1) / clusters);
+      const double ctas_on_sm = (double)(((long)clusters * s + sms - 1) / sms);
+      double cost = ctas_on_sm * tiles_per * (double)(cpw * nw) * (1.0 + 0.08 * (s > 1)) + 2.0 * tiles_per;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best.warps = nw;
+        best.ksplit = s;
+        best.clusters = clusters;
+      }
+    }
+  }
+  return best;
 }
 
 int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
@@ -97,7 +116,7 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0};
   lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
-  if (lb::gemv_mma_smem_bytes((int)m, (int)k, c.ksplit, c.mt, c.warps) > 227 * 1024)
+  if (c.warps == 0)
     return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
   return launched(lb::launch_gemv_mma(p, c, st), "w4_gemv");
 }

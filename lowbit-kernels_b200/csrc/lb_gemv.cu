@@ -1,20 +1,23 @@
-// W4A16 decode GEMV for sm_100a: y[M, N] = x[M, K] * dequant(W)[N, K]^T for M <= 16 rows.
+// W4A16 decode GEMV for sm_100a: y[M, N] = x[M, K] * dequant(W)[N, K]^T for small M.
 //
 // Role of the reference's gemv_v6 (csrc/w4_gemv.cu:327-391): reads the mma layout a model keeps
 // (lowbit/quant.py:67-78). Design:
-//   * a warp owns one 16-row tile of W and a strided set of its 128-wide K chunks; lane (g, t) streams
-//     16-byte words t of rows g and g+8 with L1-bypassing 128-bit loads (4 lanes cover a row's 64-byte chunk);
+//   * persistent CTAs (grid sized to the SM count): a CTA stages its slice of the activations once, then
+//     streams 16-row tiles of W; the warps of the CTA split each tile's 128-wide K chunks;
+//   * each warp keeps a D-deep ring of cp.async (LDGSTS) copies in shared memory: lane (g, t) copies the
+//     16-byte words t of rows g and g+8 of a chunk -- exactly the tensor-core fragment it will consume -- so
+//     bytes in flight do not depend on registers, the ring runs on across tile boundaries, and no
+//     cross-lane synchronization is needed (each lane reads back only what it copied);
 //   * the nibbles become exact fp16 integers q = u - 8 in registers (mask-OR into the 1024.0 mantissa, one
-//     f16x2 subtract or fma per pair, no integer conversion), and go straight into mma.sync m16n8k16 as the
-//     A fragment -- the mma layout is exactly that fragment, so no shuffles are needed;
-//   * activations are the B operand (up to 8 rows per n8 tile, MT tiles), staged once per CTA in shared
-//     memory in the order each lane consumes them (one 128-bit shared load per two k16 steps);
+//     f16x2 subtract or fma per pair, no integer conversion) and feed mma.sync m16n8k16 as the A fragment;
+//     activations are the B operand (n8 tiles of up to 8 rows), staged in consumption order;
 //   * each chunk's fp32 accumulator is scaled by its group scale in fp32 and folded into the running sum,
-//     so products q * x are exact and the group scale is applied without rounding the weight to fp16;
-//   * warps of a CTA split K and reduce through shared memory; for narrow or long layers a thread-block
-//     cluster splits K further and reduces through distributed shared memory (no global scratch);
+//     so products q * x are exact and the weight is never rounded to fp16;
+//   * per tile, warps publish partial sums to shared memory (double-buffered) and one warp reduces and
+//     stores; for narrow, long-K layers a thread-block cluster splits K and the reducing warp adds the
+//     ranks' partials through distributed shared memory (no global scratch, no spin-waits);
 //   * programmatic dependent launch: the kernel lets its successor launch at entry and waits for its
-//     predecessor before reading activations (optionally after issuing its first weight loads).
+//     predecessor before touching activations or outputs (optionally after starting its weight copies).
 #include <cooperative_groups.h>
 
 #include "lb_common.cuh"
@@ -24,75 +27,107 @@ namespace cg = cooperative_groups;
 
 namespace lb {
 
-// shared-memory words of activations per CTA: M rows of (chunks * 64 + 16) words (the +16 words put
-// consecutive activation rows 16 banks apart, so two rows read in one phase never collide)
+// shared-memory words of activations per row: (chunks * 64 + 16) -- the +16 words put consecutive activation
+// rows 16 banks apart, so two rows read in one phase never collide
 __host__ __device__ inline int gemv_x_row_words(int nchunks) { return nchunks * 64 + 16; }
 
-template <int MT, int NW, int U>
-__global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(GemvParams p) {
-  extern __shared__ __align__(16) uint32_t smem[];
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+struct GemvLayout {  // byte offsets inside dynamic shared memory
+  int x, ring, red, part, total;
+};
+
+__host__ __device__ inline GemvLayout gemv_layout(int M, int nl, int mt, int nw, int depth, int nsplit) {
+  GemvLayout L;
+  L.x = 0;
+  L.ring = ((M * gemv_x_row_words(nl) * 4) + 127) & ~127;
+  L.red = L.ring + nw * depth * 1024;
+  L.part = L.red + 2 * nw * mt * 512;
+  L.total = L.part + (nsplit > 1 ? 2 * nsplit * mt * 512 : 0);
+  return L;
+}
+
+template <int MT, int NW, int D>
+__global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int K = p.K, N = p.N, M = p.M;
-  const int KC = K >> 7;
+  const int KC = K >> 7, KG = K / p.G, cpg = p.G >> 7;
   const int split = blockIdx.y, nsplit = gridDim.y;
   const int c_begin = (int)((int64_t)KC * split / nsplit);
   const int c_end = (int)((int64_t)KC * (split + 1) / nsplit);
   const int nl = c_end - c_begin;
   const int row_words = gemv_x_row_words(nl);
-  const int n0 = blockIdx.x * 16;
-  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);  // tail rows re-read row N-1, never stored
-  const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * (K >> 5) + t;
-  const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * (K >> 5) + t;
-  const int KG = K / p.G, cpg = p.G >> 7;
-  const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
-  const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+  // the layout follows the largest rank's chunk count, so every rank of a cluster agrees on where rank 0's
+  // partial-sum buffer lives
+  const GemvLayout L = gemv_layout(M, (KC + nsplit - 1) / nsplit, MT, NW, D, nsplit);
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + L.x);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* part = reinterpret_cast<float*>(smem + L.part);
+  const uint32_t ring = smem_u32(smem + L.ring) + warp * (D * 1024) + lane * 16;   // + (slot * 2 + h) * 512
 
-  pdl_launch_dependents();
+  // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...; every warp walks the same job sequence:
+  // job j = (tile iteration j / cpw, chunk c_begin + warp + NW * (j % cpw))
+  const int NT = (N + 15) >> 4;
+  const int ntiles = blockIdx.x < NT ? (NT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int cpw = (nl + NW - 1) / NW;
+  const int J = ntiles * cpw;
+  const uint4* w4 = reinterpret_cast<const uint4*>(p.w);
+  const uint16_t* s16 = reinterpret_cast<const uint16_t*>(p.s);
 
-  // This warp's chunks are c_begin + warp + NW * i. Two register buffers of U chunks each alternate: the
-  // loads of one are in flight while the other is consumed, and a buffer is refilled right after use, so
-  // a warp never waits for one batch before requesting the next.
-  const int first = c_begin + warp, stride = NW * U;
-  uint4 a0[U], b0[U], a1[U], b1[U];      // buffer 0 / 1: rows g (a) and g + 8 (b)
-  uint16_t sa0[U], sb0[U], sa1[U], sb1[U];
-  auto load = [&](uint4 (&qa)[U], uint4 (&qb)[U], uint16_t (&ssa)[U], uint16_t (&ssb)[U], int c0) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + NW * u;
+  auto job_chunk = [&](int j) { return c_begin + warp + NW * (j % cpw); };
+  auto job_tile = [&](int j) { return blockIdx.x + gridDim.x * (j / cpw); };
+
+  uint16_t sra[D], srb[D];
+  // start the copies of job j into ring slot `slot` and its scales into sra/srb[slot]; always one commit group
+  auto issue = [&](int j, int slot, uint16_t& ra_s, uint16_t& rb_s) {
+    if (j < J) {
+      const int c = job_chunk(j);
       if (c < c_end) {
+        const int n0 = job_tile(j) * 16;
+        const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1
+        cp_async16(ring + (slot * 2 + 0) * 512, w4 + (size_t)ra * (K >> 5) + 4 * c + t);
+        cp_async16(ring + (slot * 2 + 1) * 512, w4 + (size_t)rb * (K >> 5) + 4 * c + t);
         const int grp = cpg == 1 ? c : c / cpg;
-        qa[u] = ldg_stream(wa + 4 * c);
-        qb[u] = ldg_stream(wb + 4 * c);
-        ssa[u] = ldg_u16(sa + grp);
-        ssb[u] = ldg_u16(sb + grp);
+        ra_s = ldg_u16(s16 + (size_t)ra * KG + grp);
+        rb_s = ldg_u16(s16 + (size_t)rb * KG + grp);
       }
     }
+    cp_async_commit();
   };
 
-  if (p.flags & kFlagEarlyWeights) {
-    // weights and scales are static model state: fetch them before the predecessor kernel finishes
-    load(a0, b0, sa0, sb0, first);
-    load(a1, b1, sa1, sb1, first + stride);
-    pdl_wait();
-  } else {
-    pdl_wait();
-    load(a0, b0, sa0, sb0, first);
-    load(a1, b1, sa1, sb1, first + stride);
-  }
+  pdl_launch_dependents();
+  const bool early = (p.flags & kFlagEarlyWeights) != 0;
+  if (!early) pdl_wait();
+#pragma unroll
+  for (int u = 0; u < D - 1; ++u) issue(u, u, sra[u], srb[u]);
+  if (early) pdl_wait();
 
-  // stage x[:, chunks c_begin..c_end) in consumption order: word ((m * row_words) + lc * 64 + qd * 16 + t * 4 + e)
+  // stage x[:, chunks c_begin..c_end) in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
   // holds the pair x[m][128 c + 8 s + 2 t .. +1] with s = 4 qd + e
   {
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x);
     const int pairs = nl * 64;
     for (int idx = threadIdx.x; idx < M * pairs; idx += NW * 32) {
-      int m = idx / pairs, pi = idx - m * pairs;
-      int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-      smem[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] =
+      const int m = idx / pairs, pi = idx - m * pairs;
+      const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
+      xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] =
           __ldg(xw + (size_t)m * (K >> 1) + (size_t)(c_begin + lc) * 64 + o);
     }
   }
   __syncthreads();
+
+  int xoff[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
 
   float acc[MT][4];
 #pragma unroll
@@ -100,103 +135,109 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(GemvParams p) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
 
-  int xoff[MT];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
+  constexpr int kTile = MT * 128;
+  int buf = 0;
 
-  auto compute = [&](const uint4 (&qa)[U], const uint4 (&qb)[U], const uint16_t (&ssa)[U],
-                     const uint16_t (&ssb)[U], int c0) {
+  for (int j0 = 0; j0 < J; j0 += D) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + NW * u;
-      if (c < c_end) {
-        const int lc = c - c_begin;
-        float d[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d[mt][i] = 0.f;
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          uint32_t w0 = (&qa[u].x)[qd], w1 = (&qb[u].x)[qd];
-          uint4 xb[MT];
+    for (int u = 0; u < D; ++u) {
+      const int j = j0 + u;
+      issue(j + D - 1, (u + D - 1) % D, sra[(u + D - 1) % D], srb[(u + D - 1) % D]);
+      cp_async_wait<D - 1>();   // the group of job j has landed (this lane's own copies)
+      if (j < J) {
+        const int c = job_chunk(j);
+        if (c < c_end) {
+          const int lc = c - c_begin;
+          const uint4 qa = *reinterpret_cast<const uint4*>(smem + (ring - smem_u32(smem)) + (u * 2 + 0) * 512);
+          const uint4 qb = *reinterpret_cast<const uint4*>(smem + (ring - smem_u32(smem)) + (u * 2 + 1) * 512);
+          float d[MT][4];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt)
-            xb[mt] = *reinterpret_cast<const uint4*>(smem + xoff[mt] + lc * 64 + qd * 16);
-          // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
-          uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
-          // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
-          w0 >>= 8;
-          w1 >>= 8;
-          f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+            for (int i = 0; i < 4; ++i) d[mt][i] = 0.f;
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+          for (int qd = 0; qd < 4; ++qd) {
+            uint32_t w0 = (&qa.x)[qd], w1 = (&qb.x)[qd];
+            uint4 xb[MT];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+              xb[mt] = *reinterpret_cast<const uint4*>(xs + xoff[mt] + lc * 64 + qd * 16);
+            // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
+            uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
+            // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
+            w0 >>= 8;
+            w1 >>= 8;
+            f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+          }
+          const float s0 = h2f_bits(sra[u]), s1 = h2f_bits(srb[u]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
+            acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
+            acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
+            acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+          }
         }
-        const float s0 = h2f_bits(ssa[u]), s1 = h2f_bits(ssb[u]);
+        if (j % cpw == cpw - 1) {
+          // end of a tile: publish, reduce in one warp, store (or hand to the cluster's rank 0)
+          const int tile = job_tile(j), it = j / cpw;
+          float* rb = red + buf * NW * kTile;
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
-          acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
-          acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
-          acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              rb[(warp * MT + mt) * 128 + i * 32 + lane] = acc[mt][i];
+              acc[mt][i] = 0.f;
+            }
+          __syncthreads();
+          const int n0 = tile * 16;
+          if (nsplit == 1) {
+            if (warp == it % NW) {
+              for (int e = lane; e < kTile; e += 32) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
+                const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+                const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+                const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
+                if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+              }
+            }
+          } else {
+            cg::cluster_group cluster = cg::this_cluster();
+            float* pb = part + buf * nsplit * kTile;
+            if (warp == it % NW) {
+              float* dst = cluster.map_shared_rank(pb, 0) + split * kTile;
+              for (int e = lane; e < kTile; e += 32) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
+                dst[e] = v;
+              }
+            }
+            cluster.sync();
+            if (split == 0 && warp == it % NW) {
+              for (int e = lane; e < kTile; e += 32) {
+                float v = 0.f;
+                for (int r = 0; r < nsplit; ++r) v += pb[r * kTile + e];
+                const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+                const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+                const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
+                if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+              }
+            }
+          }
+          buf ^= 1;
         }
       }
     }
-  };
-
-  for (int c0 = first; c0 < c_end; c0 += 2 * stride) {
-    compute(a0, b0, sa0, sb0, c0);
-    load(a0, b0, sa0, sb0, c0 + 2 * stride);
-    compute(a1, b1, sa1, sb1, c0 + stride);
-    load(a1, b1, sa1, sb1, c0 + 3 * stride);
   }
-
-  // reduce the NW warps' partial tiles: red[warp][mt][i][lane]
-  __syncthreads();  // the activation buffer is reused for the reduction
-  float* red = reinterpret_cast<float*>(smem);
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) red[((warp * MT + mt) * 4 + i) * 32 + lane] = acc[mt][i];
-  __syncthreads();
-
-  // element e of the tile is (mt = e / 128, i = e / 32 % 4, lane = e % 32); a CTA has fewer threads than
-  // a multi-tile (MT > 1) tile has elements, so threads stride over them
-  constexpr int kTile = MT * 128;
-  auto store = [&](int e, float v) {
-    const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-    const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-    const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-    if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
-  };
-  auto cta_sum = [&](int e) {
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) v += red[w * kTile + e];
-    return v;
-  };
-
-  if (nsplit > 1) {
-    // cluster split-K: every CTA writes its partial tile into its slot of rank 0's buffer; rank 0 sums the
-    // slots in rank order. The first cluster barrier makes sure rank 0 is past its main loop (the buffer
-    // overlaps its activation stage), the second that every slot has landed.
-    cg::cluster_group cluster = cg::this_cluster();
-    float* part = red + NW * kTile;  // [nsplit][kTile] in rank 0's shared memory
-    float* dst = cluster.map_shared_rank(part, 0);
-    cluster.sync();
-    for (int e = threadIdx.x; e < kTile; e += NW * 32) dst[split * kTile + e] = cta_sum(e);
-    cluster.sync();
-    if (split != 0) return;
-    for (int e = threadIdx.x; e < kTile; e += NW * 32) {
-      float v = 0.f;
-      for (int r = 0; r < nsplit; ++r) v += part[r * kTile + e];
-      store(e, v);
-    }
-  } else {
-    for (int e = threadIdx.x; e < kTile; e += NW * 32) store(e, cta_sum(e));
-  }
+  cp_async_wait<0>();
+  if (nsplit > 1) cg::this_cluster().sync();   // rank 0's buffers stay alive until every rank is done with them
 }
 
 // Compatibility GEMV for the canonical and v3 layouts (the reference's v1-v4 roles, csrc/w4_gemv.cu:38-207),
@@ -285,34 +326,31 @@ __global__ void __launch_bounds__(128) gemv_compat_kernel(GemvParams p) {
 
 // ------------------------------------------------------------------------------------------------ launchers
 
-template <int MT, int NW, int U>
-static cudaError_t launch_mma(const GemvParams& p, int nsplit, cudaStream_t st, bool pdl) {
+template <int MT, int NW, int D>
+static cudaError_t launch_stream(const GemvParams& p, const GemvConfig& c, cudaStream_t st) {
   const int KC = p.K >> 7;
-  const int max_nl = (KC + nsplit - 1) / nsplit;
-  const int tile_elems = MT * 128;
-  size_t x_bytes = (size_t)p.M * gemv_x_row_words(max_nl) * 4;
-  size_t red_bytes = (size_t)(NW + nsplit) * tile_elems * 4;
-  size_t smem = x_bytes > red_bytes ? x_bytes : red_bytes;
-  auto kern = gemv_mma_kernel<MT, NW, U>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int max_nl = (KC + c.ksplit - 1) / c.ksplit;
+  const GemvLayout L = gemv_layout(p.M, max_nl, MT, NW, D, c.ksplit);
+  auto kern = gemv_stream_kernel<MT, NW, D>;
+  if (L.total > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.N + 15) / 16, nsplit, 1);
+  cfg.gridDim = dim3(c.clusters, c.ksplit, 1);
   cfg.blockDim = dim3(NW * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (nsplit > 1) {
+  if (c.ksplit > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = nsplit;
+    attr[na].val.clusterDim.y = c.ksplit;
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
-  if (pdl) {
+  if (c.pdl) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -322,19 +360,17 @@ static cudaError_t launch_mma(const GemvParams& p, int nsplit, cudaStream_t st, 
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-size_t gemv_mma_smem_bytes(int M, int K, int nsplit, int mt, int nw) {
+size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw) {
   const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
-  size_t x_bytes = (size_t)M * gemv_x_row_words(max_nl) * 4;
-  size_t red_bytes = (size_t)(nw + nsplit) * mt * 128 * 4;
-  return x_bytes > red_bytes ? x_bytes : red_bytes;
+  return (size_t)gemv_layout(M, max_nl, mt, nw, kGemvDepth, nsplit).total;
 }
 
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st) {
-  const bool pdl = c.pdl != 0;
-#define LB_MMA(MT_, NW_)                                                 \
-  if (c.mt == MT_ && c.warps == NW_) return launch_mma<MT_, NW_, 2>(p, c.ksplit, st, pdl);
-  LB_MMA(1, 4) LB_MMA(1, 8) LB_MMA(2, 4) LB_MMA(2, 8) LB_MMA(4, 4) LB_MMA(8, 4)
-#undef LB_MMA
+#define LB_STREAM(MT_, NW_)                                                      \
+  if (c.mt == MT_ && c.warps == NW_) return launch_stream<MT_, NW_, kGemvDepth>(p, c, st);
+  LB_STREAM(1, 4) LB_STREAM(1, 8) LB_STREAM(1, 16) LB_STREAM(2, 4) LB_STREAM(2, 8) LB_STREAM(2, 16)
+  LB_STREAM(4, 4) LB_STREAM(4, 8) LB_STREAM(8, 4) LB_STREAM(8, 8)
+#undef LB_STREAM
   return cudaErrorInvalidConfiguration;
 }
 

@@ -21,14 +21,17 @@ struct GemvParams {
 };
 
 struct GemvConfig {
-  int mt;      // n8 activation tiles (1: M <= 8, 2: M <= 16)
-  int warps;   // warps per CTA (4 or 8)
-  int ksplit;  // CTAs per cluster splitting K (1..8)
-  int pdl;     // launch with programmatic stream serialization
+  int mt;        // n8 activation tiles (1: M <= 8, 2: M <= 16, 4: M <= 32, 8: M <= 64)
+  int warps;     // warps per CTA (4, 8 or 16)
+  int ksplit;    // CTAs per cluster splitting K (1..8)
+  int clusters;  // persistent CTA groups (grid.x); each walks 16-row tiles x, x + clusters, ...
+  int pdl;       // launch with programmatic stream serialization
 };
 
+constexpr int kGemvDepth = 4;  // cp.async ring depth per warp (chunks in flight)
+
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
-size_t gemv_mma_smem_bytes(int M, int K, int nsplit, int mt, int nw);
+size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw);
 cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
 
 // format kernels (lb_format.cu)
