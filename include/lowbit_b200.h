@@ -49,7 +49,8 @@ typedef enum lb_option {
   LB_OPT_EARLY_WEIGHTS = 1, /* 1: GEMV kernels fetch their first weights before waiting on the previous kernel
                                in the stream (only for weights no in-flight kernel writes); default 0 */
   LB_OPT_GEMV_KSPLIT = 2,   /* 0 (default): automatic; 1..8 forces the GEMV's K-split cluster size */
-  LB_OPT_GEMV_WARPS = 3     /* 0 (default): automatic; 4 or 8 forces the GEMV's warps per CTA */
+  LB_OPT_GEMV_WARPS = 3,    /* 0 (default): automatic; 4, 8 or 16 forces the GEMV's warps per CTA */
+  LB_OPT_GEMV_DEPTH = 4     /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
 } lb_option;
 
 /* ABI version of this header; bumped on any signature change. */

@@ -25,7 +25,8 @@ int ok() {
   return LB_OK;
 }
 
-std::atomic<int> g_opt[4] = {{1}, {0}, {0}, {0}};
+constexpr int kNumOptions = 5;
+std::atomic<int> g_opt[kNumOptions] = {{1}, {0}, {0}, {0}, {0}};
 
 int g_sm_count = 0;  // SMs of the current device (set by check_device)
 
@@ -82,13 +83,15 @@ lb::GemvConfig gemv_config(int M, int N, int K) {
   const int sms = g_sm_count > 0 ? g_sm_count : 148;
   const int nt = (N + 15) / 16, kc = K >> 7;
   const int forced_s = g_opt[LB_OPT_GEMV_KSPLIT].load(), forced_w = g_opt[LB_OPT_GEMV_WARPS].load();
+  const int forced_d = g_opt[LB_OPT_GEMV_DEPTH].load();
+  best.depth = forced_d == 4 || forced_d == 8 ? forced_d : 8;
   double best_cost = 1e30;
   for (int nw : {16, 8, 4}) {
     if (best.mt >= 4 && nw == 16) continue;
     if (forced_w && nw != forced_w) continue;
     for (int s = 1; s <= 8 && s <= kc; ++s) {
       if (forced_s && s != forced_s) continue;
-      const size_t smem = lb::gemv_smem_bytes(M, K, s, best.mt, nw);
+      const size_t smem = lb::gemv_smem_bytes(M, K, s, best.mt, nw, best.depth);
       if (smem > 227 * 1024) continue;
       int per_sm = 16 / nw;
       while (per_sm > 1 && (size_t)per_sm * smem > 220 * 1024) --per_sm;
@@ -116,8 +119,17 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0};
   lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
-  if (c.warps == 0)
-    return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
+  if (c.warps == 0) {
+    // the staged activations do not fit in shared memory: run the rows in two halves (each reads W once)
+    if (m == 1)
+      return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
+    const int64_t h = (m / 2 + 7) & ~7LL;   // keep the first half a whole number of 8-row tiles
+    const int64_t m0 = h < m ? h : m / 2;
+    int rc = run_gemv_mma(x, w, s, y, m0, n, k, group, st);
+    if (rc) return rc;
+    return run_gemv_mma(static_cast<const char*>(x) + m0 * k * 2, w, s, static_cast<char*>(y) + m0 * n * 2, m - m0,
+                        n, k, group, st);
+  }
   return launched(lb::launch_gemv_mma(p, c, st), "w4_gemv");
 }
 
@@ -141,12 +153,12 @@ const char* lb_status_string(int status) {
 const char* lb_last_error(void) { return g_err; }
 
 int lb_set_option(int option, int value) {
-  if (option < 0 || option > 3) return -1;
+  if (option < 0 || option >= kNumOptions) return -1;
   return g_opt[option].exchange(value);
 }
 
 int lb_get_option(int option) {
-  if (option < 0 || option > 3) return -1;
+  if (option < 0 || option >= kNumOptions) return -1;
   return g_opt[option].load();
 }
 

@@ -360,14 +360,15 @@ static cudaError_t launch_stream(const GemvParams& p, const GemvConfig& c, cudaS
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw) {
+size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth) {
   const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
-  return (size_t)gemv_layout(M, max_nl, mt, nw, kGemvDepth, nsplit).total;
+  return (size_t)gemv_layout(M, max_nl, mt, nw, depth, nsplit).total;
 }
 
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st) {
-#define LB_STREAM(MT_, NW_)                                                      \
-  if (c.mt == MT_ && c.warps == NW_) return launch_stream<MT_, NW_, kGemvDepth>(p, c, st);
+#define LB_STREAM(MT_, NW_)                                                              \
+  if (c.mt == MT_ && c.warps == NW_)                                                     \
+    return c.depth == 8 ? launch_stream<MT_, NW_, 8>(p, c, st) : launch_stream<MT_, NW_, 4>(p, c, st);
   LB_STREAM(1, 4) LB_STREAM(1, 8) LB_STREAM(1, 16) LB_STREAM(2, 4) LB_STREAM(2, 8) LB_STREAM(2, 16)
   LB_STREAM(4, 4) LB_STREAM(4, 8) LB_STREAM(8, 4) LB_STREAM(8, 8)
 #undef LB_STREAM

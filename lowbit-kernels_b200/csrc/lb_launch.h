@@ -25,13 +25,12 @@ struct GemvConfig {
   int warps;     // warps per CTA (4, 8 or 16)
   int ksplit;    // CTAs per cluster splitting K (1..8)
   int clusters;  // persistent CTA groups (grid.x); each walks 16-row tiles x, x + clusters, ...
+  int depth;     // cp.async ring depth per warp (chunks in flight): 4 or 8
   int pdl;       // launch with programmatic stream serialization
 };
 
-constexpr int kGemvDepth = 4;  // cp.async ring depth per warp (chunks in flight)
-
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
-size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw);
+size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth);
 cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
 
 // format kernels (lb_format.cu)
