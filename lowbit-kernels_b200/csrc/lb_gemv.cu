@@ -75,52 +75,61 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
   const uint32_t ring = smem_u32(smem + L.ring) + warp * (D * 1024) + lane * 16;   // + (slot * 2 + h) * 512
 
   // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...; every warp walks the same job sequence:
-  // job j = (tile iteration j / cpw, chunk c_begin + warp + NW * (j % cpw))
+  // job = (tile iteration, slot ci < cpw) -> chunk c_begin + warp + NW * ci. Positions advance by counters
+  // (no integer division in the loop).
   const int NT = (N + 15) >> 4;
   const int ntiles = blockIdx.x < NT ? (NT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int cpw = (nl + NW - 1) / NW;
   const int J = ntiles * cpw;
   const uint4* w4 = reinterpret_cast<const uint4*>(p.w);
   const uint16_t* s16 = reinterpret_cast<const uint16_t*>(p.s);
+  const size_t row_stride = (size_t)(K >> 5);   // uint4 per row
+  const int c_warp = c_begin + warp;
 
-  auto job_chunk = [&](int j) { return c_begin + warp + NW * (j % cpw); };
-  auto job_tile = [&](int j) { return blockIdx.x + gridDim.x * (j / cpw); };
+  struct Cursor {   // a job position: tile iteration and slot
+    int it, ci;
+    __device__ void next(int cpw_) {
+      if (++ci == cpw_) { ci = 0; ++it; }
+    }
+  };
 
   uint16_t sra[D], srb[D];
-  // start the copies of job j into ring slot `slot` and its scales into sra/srb[slot]; always one commit group
-  auto issue = [&](int j, int slot, uint16_t& ra_s, uint16_t& rb_s) {
-    if (j < J) {
-      const int c = job_chunk(j);
+  Cursor iss{0, 0};   // next job to issue
+  // start the copies of the job at `iss` into ring slot `slot` and its scales into ra_s/rb_s; always one group
+  auto issue = [&](int slot, uint16_t& ra_s, uint16_t& rb_s) {
+    if (iss.it < ntiles) {
+      const int c = c_warp + NW * iss.ci;
       if (c < c_end) {
-        const int n0 = job_tile(j) * 16;
+        const int n0 = (blockIdx.x + gridDim.x * iss.it) * 16;
         const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1
-        cp_async16(ring + (slot * 2 + 0) * 512, w4 + (size_t)ra * (K >> 5) + 4 * c + t);
-        cp_async16(ring + (slot * 2 + 1) * 512, w4 + (size_t)rb * (K >> 5) + 4 * c + t);
+        cp_async16(ring + (slot * 2 + 0) * 512, w4 + (size_t)ra * row_stride + 4 * c + t);
+        cp_async16(ring + (slot * 2 + 1) * 512, w4 + (size_t)rb * row_stride + 4 * c + t);
         const int grp = cpg == 1 ? c : c / cpg;
         ra_s = ldg_u16(s16 + (size_t)ra * KG + grp);
         rb_s = ldg_u16(s16 + (size_t)rb * KG + grp);
       }
     }
     cp_async_commit();
+    iss.next(cpw);
   };
 
   pdl_launch_dependents();
   const bool early = (p.flags & kFlagEarlyWeights) != 0;
   if (!early) pdl_wait();
 #pragma unroll
-  for (int u = 0; u < D - 1; ++u) issue(u, u, sra[u], srb[u]);
+  for (int u = 0; u < D - 1; ++u) issue(u, sra[u], srb[u]);
   if (early) pdl_wait();
 
   // stage x[:, chunks c_begin..c_end) in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
   // holds the pair x[m][128 c + 8 s + 2 t .. +1] with s = 4 qd + e
   {
-    const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x) + (size_t)c_begin * 64;
     const int pairs = nl * 64;
-    for (int idx = threadIdx.x; idx < M * pairs; idx += NW * 32) {
-      const int m = idx / pairs, pi = idx - m * pairs;
-      const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-      xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] =
-          __ldg(xw + (size_t)m * (K >> 1) + (size_t)(c_begin + lc) * 64 + o);
+    for (int m = 0; m < M; ++m) {
+      for (int pi = threadIdx.x; pi < pairs; pi += NW * 32) {
+        const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
+        xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = __ldg(xw + (size_t)m * (K >> 1) + pi);
+      }
     }
   }
   __syncthreads();
@@ -137,19 +146,74 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
 
   constexpr int kTile = MT * 128;
   int buf = 0;
+  Cursor cur{0, 0};   // job being computed
+
+  // end of a tile: publish the warps' partial sums, reduce in one warp, store (or hand to the cluster's rank 0)
+  auto tile_end = [&](int it, int& b, float (&a)[MT][4]) {
+    const int n0 = (blockIdx.x + gridDim.x * it) * 16;
+    float* rb = red + b * NW * kTile;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        rb[(warp * MT + mt) * 128 + i * 32 + lane] = a[mt][i];
+        a[mt][i] = 0.f;
+      }
+    __syncthreads();
+    const bool reducer = warp == (it & (NW - 1));
+    auto store = [&](int e, float v) {
+      const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+      const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+      const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
+      if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+    };
+    if (nsplit == 1) {
+      if (reducer) {
+#pragma unroll
+        for (int e = lane; e < kTile; e += 32) {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
+          store(e, v);
+        }
+      }
+    } else {
+      cg::cluster_group cluster = cg::this_cluster();
+      float* pb = part + b * nsplit * kTile;
+      if (reducer) {
+        float* dst = cluster.map_shared_rank(pb, 0) + split * kTile;
+#pragma unroll
+        for (int e = lane; e < kTile; e += 32) {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
+          dst[e] = v;
+        }
+      }
+      cluster.sync();
+      if (split == 0 && reducer) {
+        for (int e = lane; e < kTile; e += 32) {
+          float v = 0.f;
+          for (int r = 0; r < nsplit; ++r) v += pb[r * kTile + e];
+          store(e, v);
+        }
+      }
+    }
+    b ^= 1;
+  };
+  const uint8_t* ring_ptr = smem + (ring - smem_u32(smem));
 
   for (int j0 = 0; j0 < J; j0 += D) {
 #pragma unroll
     for (int u = 0; u < D; ++u) {
-      const int j = j0 + u;
-      issue(j + D - 1, (u + D - 1) % D, sra[(u + D - 1) % D], srb[(u + D - 1) % D]);
-      cp_async_wait<D - 1>();   // the group of job j has landed (this lane's own copies)
-      if (j < J) {
-        const int c = job_chunk(j);
+      issue((u + D - 1) % D, sra[(u + D - 1) % D], srb[(u + D - 1) % D]);
+      cp_async_wait<D - 1>();   // the group of this job has landed (this lane's own copies)
+      if (cur.it < ntiles) {
+        const int c = c_warp + NW * cur.ci;
         if (c < c_end) {
           const int lc = c - c_begin;
-          const uint4 qa = *reinterpret_cast<const uint4*>(smem + (ring - smem_u32(smem)) + (u * 2 + 0) * 512);
-          const uint4 qb = *reinterpret_cast<const uint4*>(smem + (ring - smem_u32(smem)) + (u * 2 + 1) * 512);
+          const uint4 qa = *reinterpret_cast<const uint4*>(ring_ptr + (u * 2 + 0) * 512);
+          const uint4 qb = *reinterpret_cast<const uint4*>(ring_ptr + (u * 2 + 1) * 512);
           float d[MT][4];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt)
@@ -182,58 +246,9 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
             acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
           }
         }
-        if (j % cpw == cpw - 1) {
-          // end of a tile: publish, reduce in one warp, store (or hand to the cluster's rank 0)
-          const int tile = job_tile(j), it = j / cpw;
-          float* rb = red + buf * NW * kTile;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              rb[(warp * MT + mt) * 128 + i * 32 + lane] = acc[mt][i];
-              acc[mt][i] = 0.f;
-            }
-          __syncthreads();
-          const int n0 = tile * 16;
-          if (nsplit == 1) {
-            if (warp == it % NW) {
-              for (int e = lane; e < kTile; e += 32) {
-                float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
-                const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-                const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-                const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-                if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
-              }
-            }
-          } else {
-            cg::cluster_group cluster = cg::this_cluster();
-            float* pb = part + buf * nsplit * kTile;
-            if (warp == it % NW) {
-              float* dst = cluster.map_shared_rank(pb, 0) + split * kTile;
-              for (int e = lane; e < kTile; e += 32) {
-                float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
-                dst[e] = v;
-              }
-            }
-            cluster.sync();
-            if (split == 0 && warp == it % NW) {
-              for (int e = lane; e < kTile; e += 32) {
-                float v = 0.f;
-                for (int r = 0; r < nsplit; ++r) v += pb[r * kTile + e];
-                const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-                const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-                const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-                if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
-              }
-            }
-          }
-          buf ^= 1;
-        }
+        if (cur.ci == cpw - 1) tile_end(cur.it, buf, acc);
       }
+      cur.next(cpw);
     }
   }
   cp_async_wait<0>();
