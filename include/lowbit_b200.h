@@ -50,7 +50,8 @@ typedef enum lb_option {
                                in the stream (only for weights no in-flight kernel writes); default 0 */
   LB_OPT_GEMV_KSPLIT = 2,   /* 0 (default): automatic; 1..8 forces the GEMV's K-split cluster size */
   LB_OPT_GEMV_WARPS = 3,    /* 0 (default): automatic; 4, 8 or 16 forces the GEMV's warps per CTA */
-  LB_OPT_GEMV_DEPTH = 4     /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
+  LB_OPT_GEMV_DEPTH = 4,    /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
+  LB_OPT_GEMV_KERNEL = 5    /* 0 (default): automatic; 1 the per-warp copy-ring GEMV; 2 the bulk-copy GEMV */
 } lb_option;
 
 /* ABI version of this header; bumped on any signature change. */
@@ -60,6 +61,11 @@ LB_API int lb_abi_version(void);
 LB_API const char* lb_status_string(int status);
 /* message of the last failed call on this host thread ("" after a successful call) */
 LB_API const char* lb_last_error(void);
+
+/* Device-side status of the current device: nonzero when a kernel's bounded wait gave up (a kernel bug, never
+ * expected), in which case that kernel's output is undefined. Synchronizes the device. */
+LB_API int lb_device_error(void);
+LB_API void lb_clear_device_error(void);
 
 /* process-wide launch options (lb_option); returns the previous value, or -1 for an unknown option */
 LB_API int lb_set_option(int option, int value);

@@ -25,8 +25,8 @@ int ok() {
   return LB_OK;
 }
 
-constexpr int kNumOptions = 5;
-std::atomic<int> g_opt[kNumOptions] = {{1}, {0}, {0}, {0}, {0}};
+constexpr int kNumOptions = 6;
+std::atomic<int> g_opt[kNumOptions] = {{1}, {0}, {0}, {0}, {0}, {0}};
 
 int g_sm_count = 0;  // SMs of the current device (set by check_device)
 
@@ -118,6 +118,13 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                  int64_t group, cudaStream_t st) {
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0};
+  const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
+  if (kernel != 1 && m <= 16 && lb::gemv_tma_smem_bytes((int)m, (int)k) <= 227 * 1024) {
+    // bulk-copy pipeline: one CTA per SM, each over a contiguous range of 16-row tiles
+    const int sms = g_sm_count > 0 ? g_sm_count : 148;
+    const int nt = (int)((n + 15) / 16);
+    return launched(lb::launch_gemv_tma(p, nt < sms ? nt : sms, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemv");
+  }
   lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
   if (c.warps == 0) {
     // the staged activations do not fit in shared memory: run the rows in two halves (each reads W once)
@@ -151,6 +158,10 @@ const char* lb_status_string(int status) {
 }
 
 const char* lb_last_error(void) { return g_err; }
+
+int lb_device_error(void) { return lb::tma_device_error(); }
+
+void lb_clear_device_error(void) { lb::tma_clear_device_error(); }
 
 int lb_set_option(int option, int value) {
   if (option < 0 || option >= kNumOptions) return -1;

@@ -30,6 +30,12 @@ struct GemvConfig {
 };
 
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
+
+// bulk-copy pipeline GEMV (lb_gemv_tma.cu): M <= 16, one CTA per SM over contiguous tile ranges
+cudaError_t launch_gemv_tma(const GemvParams& p, int ctas, bool pdl, cudaStream_t st);
+size_t gemv_tma_smem_bytes(int M, int K);
+int tma_device_error();          // nonzero after a bounded wait gave up (synchronizes)
+void tma_clear_device_error();
 size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth);
 cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
 

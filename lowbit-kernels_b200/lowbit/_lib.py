@@ -15,7 +15,7 @@ import torch
 
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblowbit_b200.so"
 LAYOUT_IDS = {"canonical": 0, "v3": 1, "mma": 2}
-OPTIONS = {"pdl": 0, "early_weights": 1, "gemv_ksplit": 2, "gemv_warps": 3, "gemv_depth": 4}
+OPTIONS = {"pdl": 0, "early_weights": 1, "gemv_ksplit": 2, "gemv_warps": 3, "gemv_depth": 4, "gemv_kernel": 5}
 
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
@@ -24,6 +24,8 @@ SIGNATURES = {
     "lb_abi_version": ([], _I),
     "lb_status_string": ([_I], ctypes.c_char_p),
     "lb_last_error": ([], ctypes.c_char_p),
+    "lb_device_error": ([], _I),
+    "lb_clear_device_error": ([], None),
     "lb_set_option": ([_I, _I], _I),
     "lb_get_option": ([_I], _I),
     "lb_w4_gemv": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P], _I),

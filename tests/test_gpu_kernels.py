@@ -158,6 +158,22 @@ def test_v6_gemv_parity(layers, name, m):
     check_output(y, ref_y(x, packed, scales, 128), f"v6 {name} M={m}")
 
 
+@pytest.mark.parametrize("kernel", [1, 2])
+@pytest.mark.parametrize("name", ["0.5b.kv", "1.5b.up", "3b.down", "odd_n", "tiny", "k128"])
+@pytest.mark.parametrize("m", [1, 7, 16])
+def test_both_gemv_kernels(layers, kernel, name, m):
+    """The copy-ring GEMV (1) and the bulk-copy GEMV (2) each against the oracle, whatever the dispatch picks."""
+    k, n, w, packed, scales, wq = layers[name]
+    x = x_for(m, k, k + n + 5 * m)
+    e = ops.ext()
+    prev = e.set_option("gemv_kernel", kernel)
+    try:
+        y = ops.gemv(x.cuda(), wq, 6 if m <= 8 else 5)
+    finally:
+        e.set_option("gemv_kernel", prev)
+    check_output(y, ref_y(x, packed, scales, 128), f"kernel {kernel} {name} M={m}")
+
+
 @pytest.mark.parametrize("name", [s[0] for s in SHAPES + EDGE])
 @pytest.mark.parametrize("m", [1, 4, 12, 16, 33, 48, 64])
 def test_v5_gemm_parity(layers, name, m):
@@ -324,3 +340,9 @@ def test_w4linear_matches_fake_quant_linear():
         assert y.shape == (*shape[:-1], 1000)
         rel = ((y.float() - yf.float()).abs().max() / yf.float().pow(2).mean().sqrt()).item()
         assert rel < 5e-3, (shape, rel)
+
+
+def test_no_kernel_wait_gave_up():
+    """Every bounded wait in the kernels completed (the device error word is still zero)."""
+    torch.cuda.synchronize()
+    assert ops.ext().lib.lb_device_error() == 0
