@@ -114,16 +114,41 @@ lb::GemvConfig gemv_config(int M, int N, int K) {
   return best;
 }
 
+// One-shot GEMV tiling: a CTA is one 16-row tile and a K range. K is split over a cluster of S CTAs when the
+// tiles alone would not cover the SMs or a CTA's share would exceed ~32 KB of weights (long-K layers); the
+// range's chunks are spread over NW warps with at most CPW each (CPW * 8 registers of weights per thread).
+lb::OneshotConfig oneshot_config(int M, int N, int K) {
+  lb::OneshotConfig c{0, 0, 0, g_opt[LB_OPT_PDL].load()};
+  const int sms = g_sm_count > 0 ? g_sm_count : 148;
+  const int nt = (N + 15) / 16, kc = K >> 7;
+  int s = 1;
+  while (s < 8 && s * 2 <= kc && ((kc + s - 1) / s > 32 || nt * s < sms)) ++s;
+  const int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
+  if (forced >= 1 && forced <= 8 && forced <= kc) s = forced;
+  const int nl = (kc + s - 1) / s;
+  int cpw = nl <= 16 ? 2 : nl <= 64 ? 4 : 8;
+  int nw = (nl + cpw - 1) / cpw;
+  const int fw = g_opt[LB_OPT_GEMV_WARPS].load();
+  if (fw >= 1 && fw <= 16) {
+    nw = fw;
+    cpw = (nl + nw - 1) / nw <= 2 ? 2 : (nl + nw - 1) / nw <= 4 ? 4 : 8;
+  }
+  if (nw > 16 || (long)nw * cpw < nl) return c;
+  if (lb::oneshot_smem_bytes(M, K, s, nw) > 200 * 1024) return c;
+  c.warps = nw;
+  c.cpw = cpw;
+  c.ksplit = s;
+  return c;
+}
+
 int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
                  int64_t group, cudaStream_t st) {
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0};
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
-  if (kernel != 1 && m <= 16 && lb::gemv_tma_smem_bytes((int)m, (int)k) <= 227 * 1024) {
-    // bulk-copy pipeline: one CTA per SM, each over a contiguous range of 16-row tiles
-    const int sms = g_sm_count > 0 ? g_sm_count : 148;
-    const int nt = (int)((n + 15) / 16);
-    return launched(lb::launch_gemv_tma(p, nt < sms ? nt : sms, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemv");
+  if (kernel != 1 && m <= 16) {
+    const lb::OneshotConfig c = oneshot_config((int)m, (int)n, (int)k);
+    if (c.warps > 0) return launched(lb::launch_gemv_oneshot(p, c, st), "w4_gemv");
   }
   lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
   if (c.warps == 0) {
@@ -159,9 +184,9 @@ const char* lb_status_string(int status) {
 
 const char* lb_last_error(void) { return g_err; }
 
-int lb_device_error(void) { return lb::tma_device_error(); }
+int lb_device_error(void) { return lb::device_error(); }
 
-void lb_clear_device_error(void) { lb::tma_clear_device_error(); }
+void lb_clear_device_error(void) { lb::clear_device_error(); }
 
 int lb_set_option(int option, int value) {
   if (option < 0 || option >= kNumOptions) return -1;

@@ -255,6 +255,205 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
   if (nsplit > 1) cg::this_cluster().sync();   // rank 0's buffers stay alive until every rank is done with them
 }
 
+// One-shot GEMV (M <= 16), the decode path. One CTA owns one 16-row tile and a K range (a cluster of S CTAs
+// splits long K); its warps split the range's chunks, at most CPW each. At entry every thread issues ALL of
+// its weight and scale loads (register destinations, L1 bypassed) -- before waiting on the previous kernel
+// when the weights are known static -- so each CTA has its whole share in flight at once and the next
+// kernel's CTAs, which launch early under programmatic dependent launch and fit beside this one's small
+// CTAs, do the same while this kernel computes. Then activations are staged in consumption order, each
+// chunk runs through mma.sync (exact integer weights, fp32 accumulate, fp32 group-scale fold), warps reduce
+// through shared memory, cluster ranks through distributed shared memory, and rank 0 stores.
+template <int MT, int CPW>
+__global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
+  const int NW = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int K = p.K, N = p.N, M = p.M;
+  const int KC = K >> 7, KG = K / p.G, cpg = p.G >> 7;
+  const int split = blockIdx.y, nsplit = gridDim.y;
+  const int c_begin = (int)((int64_t)KC * split / nsplit);
+  const int c_end = (int)((int64_t)KC * (split + 1) / nsplit);
+  const int nl = c_end - c_begin;
+  const int row_words = gemv_x_row_words(nl);
+  const int n0 = blockIdx.x * 16;
+  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1, never stored
+  const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * (K >> 5) + t;
+  const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * (K >> 5) + t;
+  const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
+  const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+  const int c_warp = c_begin + warp;
+
+  uint4 qa[CPW], qb[CPW];
+  uint16_t ssa[CPW], ssb[CPW];
+  pdl_launch_dependents();
+  const bool early = (p.flags & kFlagEarlyWeights) != 0;
+  if (!early) pdl_wait();
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = c_warp + NW * i;
+    if (c < c_end) {
+      const int grp = cpg == 1 ? c : c / cpg;
+      qa[i] = ldg_stream(wa + 4 * c);
+      qb[i] = ldg_stream(wb + 4 * c);
+      ssa[i] = ldg_u16(sa + grp);
+      ssb[i] = ldg_u16(sb + grp);
+    }
+  }
+  if (early) pdl_wait();
+
+  // activations of this K range in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
+  // holds the pair x[m][128 c + 8 s + 2 t .. +1], s = 4 qd + e
+  {
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x) + (size_t)c_begin * 64;
+    const int pairs = nl * 64;
+    for (int m = 0; m < M; ++m)
+      for (int pi = threadIdx.x; pi < pairs; pi += blockDim.x) {
+        const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
+        sw[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = __ldg(xw + (size_t)m * (K >> 1) + pi);
+      }
+  }
+  __syncthreads();
+
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+  int xoff[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
+
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = c_warp + NW * i;
+    if (c < c_end) {
+      const int lc = c - c_begin;
+      float d[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[mt][j] = 0.f;
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        uint32_t w0 = (&qa[i].x)[qd], w1 = (&qb[i].x)[qd];
+        uint4 xb[MT];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          xb[mt] = *reinterpret_cast<const uint4*>(sw + xoff[mt] + lc * 64 + qd * 16);
+        // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
+        uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
+        // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
+        w0 >>= 8;
+        w1 >>= 8;
+        f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+      }
+      const float s0 = h2f_bits(ssa[i]), s1 = h2f_bits(ssb[i]);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
+        acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
+        acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
+        acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+      }
+    }
+  }
+
+  // reduce the warps' partial tiles: red[warp][mt][i][lane] (the activation buffer is free again)
+  constexpr int kTile = MT * 128;
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(sw);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp * kTile + mt * 128 + i * 32 + lane] = acc[mt][i];
+  __syncthreads();
+  auto store = [&](int e, float v) {
+    const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+    const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+    const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
+    if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+  };
+  auto cta_sum = [&](int e) {
+    float v = 0.f;
+    for (int w = 0; w < NW; ++w) v += red[w * kTile + e];
+    return v;
+  };
+  if (nsplit == 1) {
+    for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, cta_sum(e));
+    return;
+  }
+  // cluster split-K: each rank writes its partial tile into its slot of rank 0's buffer (after a cluster
+  // barrier: the buffer follows rank 0's reduction area), a second barrier publishes the slots, rank 0 adds
+  // them in rank order
+  cg::cluster_group cluster = cg::this_cluster();
+  float* part = red + NW * kTile;
+  float* dst = cluster.map_shared_rank(part, 0) + split * kTile;
+  cluster.sync();
+  for (int e = threadIdx.x; e < kTile; e += blockDim.x) dst[e] = cta_sum(e);
+  cluster.sync();
+  if (split == 0) {
+    for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
+      float v = 0.f;
+      for (int r = 0; r < nsplit; ++r) v += part[r * kTile + e];
+      store(e, v);
+    }
+  }
+}
+
+template <int MT, int CPW>
+static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
+  auto kern = gemv_oneshot_kernel<MT, CPW>;
+  const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + 15) / 16, c.ksplit, 1);
+  cfg.blockDim = dim3(c.warps * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (c.ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = c.ksplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (c.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw) {
+  const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
+  const int mt = M <= 8 ? 1 : 2;
+  const size_t x_bytes = (size_t)M * gemv_x_row_words(max_nl) * 4;
+  const size_t red_bytes = (size_t)(nw + (nsplit > 1 ? nsplit : 0)) * mt * 128 * 4;
+  return x_bytes > red_bytes ? x_bytes : red_bytes;
+}
+
+cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
+  const int mt = p.M <= 8 ? 1 : 2;
+#define LB_ONESHOT(MT_, CPW_) \
+  if (mt == MT_ && c.cpw == CPW_) return launch_oneshot_t<MT_, CPW_>(p, c, st);
+  LB_ONESHOT(1, 2) LB_ONESHOT(1, 4) LB_ONESHOT(1, 8) LB_ONESHOT(2, 2) LB_ONESHOT(2, 4) LB_ONESHOT(2, 8)
+#undef LB_ONESHOT
+  return cudaErrorInvalidConfiguration;
+}
+
 // Compatibility GEMV for the canonical and v3 layouts (the reference's v1-v4 roles, csrc/w4_gemv.cu:38-207),
 // any group size that is a multiple of 32, M <= 8: a warp owns R rows; lanes stride over 32-weight words;
 // exact integer values times activations accumulate in fp32, scaled once per 32-weight piece.

@@ -31,11 +31,19 @@ struct GemvConfig {
 
 cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
 
-// bulk-copy pipeline GEMV (lb_gemv_tma.cu): M <= 16, one CTA per SM over contiguous tile ranges
-cudaError_t launch_gemv_tma(const GemvParams& p, int ctas, bool pdl, cudaStream_t st);
-size_t gemv_tma_smem_bytes(int M, int K);
-int tma_device_error();          // nonzero after a bounded wait gave up (synchronizes)
-void tma_clear_device_error();
+// one-shot GEMV (M <= 16): one 16-row tile per CTA, all weight loads issued at entry
+struct OneshotConfig {
+  int warps;   // warps per CTA (1..16)
+  int cpw;     // most chunks per warp: 2, 4 or 8
+  int ksplit;  // CTAs per cluster splitting K (1..8)
+  int pdl;
+};
+cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
+size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw);
+
+// device status word (lb_status.cu): nonzero after a bounded wait in a kernel gave up
+int device_error();   // synchronizes
+void clear_device_error();
 size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth);
 cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
 
