@@ -63,10 +63,24 @@ __device__ __forceinline__ uint16_t ldg_u16(const void* p) {
 
 __device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// Load of data a previous kernel in the stream may have just written (activations): cached in L2 only, so no
+// stale L1 line from before the programmatic-dependency wait can be hit.
+__device__ __forceinline__ uint32_t ldg_cg_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // Programmatic dependent launch: let the next kernel in the stream launch, and wait for the previous one.
 // Both are no-ops when the launch carries no programmatic dependency.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// The wait behind a branch on a kernel argument that is always nonzero: the compiler may legally sink loads
+// issued before an unconditional wait below it (which serializes them behind the previous kernel); it does
+// not move them across the branch, so weight loads issued first really are in flight during the wait.
+__device__ __forceinline__ void pdl_wait_after_loads(int guard) {
+  if (guard) pdl_wait();
+}
 
 // D += A * B, m16n8k16, f16 inputs, f32 accumulators (PTX ISA fragment layout: lane = 4g + t;
 // a0 = A[g][2t..2t+1], a1 = A[g+8][2t..], a2 = A[g][2t+8..], a3 = A[g+8][2t+8..]; b0 = B[2t..][g], b1 = B[2t+8..][g];

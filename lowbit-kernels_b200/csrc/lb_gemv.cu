@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
   if (!early) pdl_wait();
 #pragma unroll
   for (int u = 0; u < D - 1; ++u) issue(u, sra[u], srb[u]);
-  if (early) pdl_wait();
+  if (early) pdl_wait_after_loads(p.wait_guard);
 
   // stage x[:, chunks c_begin..c_end) in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
   // holds the pair x[m][128 c + 8 s + 2 t .. +1] with s = 4 qd + e
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
     for (int m = 0; m < M; ++m) {
       for (int pi = threadIdx.x; pi < pairs; pi += NW * 32) {
         const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-        xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = __ldg(xw + (size_t)m * (K >> 1) + pi);
+        xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
       }
     }
   }
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
 // CTAs, do the same while this kernel computes. Then activations are staged in consumption order, each
 // chunk runs through mma.sync (exact integer weights, fp32 accumulate, fp32 group-scale fold), warps reduce
 // through shared memory, cluster ranks through distributed shared memory, and rank 0 stores.
-template <int MT, int CPW>
+template <int MT, int CPW, bool EARLY>
 __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
@@ -287,8 +287,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   uint4 qa[CPW], qb[CPW];
   uint16_t ssa[CPW], ssb[CPW];
   pdl_launch_dependents();
-  const bool early = (p.flags & kFlagEarlyWeights) != 0;
-  if (!early) pdl_wait();
+  if (!EARLY) pdl_wait();
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
@@ -300,7 +299,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
       ssb[i] = ldg_u16(sb + grp);
     }
   }
-  if (early) pdl_wait();
+  if (EARLY) pdl_wait_after_loads(p.wait_guard);
 
   // activations of this K range in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
   // holds the pair x[m][128 c + 8 s + 2 t .. +1], s = 4 qd + e
@@ -310,7 +309,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int m = 0; m < M; ++m)
       for (int pi = threadIdx.x; pi < pairs; pi += blockDim.x) {
         const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-        sw[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = __ldg(xw + (size_t)m * (K >> 1) + pi);
+        sw[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
       }
   }
   __syncthreads();
@@ -407,7 +406,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
 
 template <int MT, int CPW>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
-  auto kern = gemv_oneshot_kernel<MT, CPW>;
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, CPW, true> : gemv_oneshot_kernel<MT, CPW, false>;
   const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -509,7 +508,10 @@ __global__ void __launch_bounds__(128) gemv_compat_kernel(GemvParams p) {
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) {
-        uint4 xv = __ldg(x4 + (size_t)m * (K >> 3) + 4 * c + i);
+        uint4 xv;
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(xv.x), "=r"(xv.y), "=r"(xv.z), "=r"(xv.w)
+                     : "l"(x4 + (size_t)m * (K >> 3) + 4 * c + i));
         const __half2* xh = reinterpret_cast<const __half2*>(&xv);
         float xf[8];
 #pragma unroll

@@ -18,6 +18,7 @@ struct GemvParams {
   __half* y;      // fp16 [M, N]
   int M, N, K, G;
   int flags;
+  int wait_guard;  // always 1 (see pdl_wait_after_loads)
 };
 
 struct GemvConfig {
