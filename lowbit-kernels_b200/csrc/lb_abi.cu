@@ -126,14 +126,13 @@ lb::OneshotConfig oneshot_config(int M, int N, int K) {
   const int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
   if (forced >= 1 && forced <= 8 && forced <= kc) s = forced;
   const int nl = (kc + s - 1) / s;
-  int cpw = nl <= 16 ? 2 : nl <= 64 ? 4 : 8;
-  int nw = (nl + cpw - 1) / cpw;
+  int nw = (nl + 3) / 4;
   const int fw = g_opt[LB_OPT_GEMV_WARPS].load();
-  if (fw >= 1 && fw <= 16) {
-    nw = fw;
-    cpw = (nl + nw - 1) / nw <= 2 ? 2 : (nl + nw - 1) / nw <= 4 ? 4 : 8;
-  }
-  if (nw > 16 || (long)nw * cpw < nl) return c;
+  if (fw >= 1 && fw <= 16) nw = fw;
+  if (nw > 16) nw = 16;
+  const int per = (nl + nw - 1) / nw;
+  const int cpw = per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 0;
+  if (cpw == 0) return c;
   if (lb::oneshot_smem_bytes(M, K, s, nw) > 200 * 1024) return c;
   c.warps = nw;
   c.cpw = cpw;

@@ -42,7 +42,7 @@ struct OneshotConfig {
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw);
 
-// device status word (lb_status.cu): nonzero after a bounded wait in a kernel gave up
+// device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
 int device_error();   // synchronizes
 void clear_device_error();
 size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth);
