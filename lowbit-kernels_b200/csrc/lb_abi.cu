@@ -143,7 +143,8 @@ lb::OneshotConfig oneshot_config(int M, int N, int K) {
 int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
                  int64_t group, cudaStream_t st) {
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
-                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1};
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
+                   (int)(group / 128)};
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
   if (kernel != 1 && m <= 16) {
     const lb::OneshotConfig c = oneshot_config((int)m, (int)n, (int)k);
@@ -211,7 +212,8 @@ int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_
   if ((rc = check_device())) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (version == 6) return run_gemv_mma(x, w, scales, y, m, n, k, group, st);
-  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group, 0, 1};
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group, 0, 1,
+                   (int)(k / group), (int)(group / 128)};
   int R = rows_per_warp ? rows_per_warp : (n >= 512 ? 4 : (m >= 4 ? 2 : 1));
   return launched(lb::launch_gemv_compat(p, R, version >= 3, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemv");
 }

@@ -256,14 +256,13 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
 }
 
 // One-shot GEMV (M <= 16), the decode path. One CTA owns one 16-row tile and a K range (a cluster of S CTAs
-// splits long K). At entry one warp issues the tile's weights as 16 bulk copies (one per row, into padded
-// shared-memory rows) completing on one mbarrier, and every lane loads the scales of its chunks -- before the
-// programmatic-dependency wait when the weights are known static. The CTA's footprint is then a few KB of
-// registers and its share of weights in shared memory, so the next kernel's CTAs, which launch early, fit
-// beside it and put their own weights in flight while this one computes. After the wait: activations are
-// staged in consumption order, the warps split the range's chunks through mma.sync (exact integer weights,
-// fp32 accumulate, fp32 group-scale fold), reduce through shared memory, cluster ranks through distributed
-// shared memory, and rank 0 stores. The one mbarrier wait is bounded and reports a timeout on the status word.
+// splits long K); its warps split the range's chunks, at most CPW each. At entry every thread issues ALL of
+// its weight and scale loads (register destinations, L1 bypassed) -- before waiting on the previous kernel
+// when the weights are known static -- so each CTA has its whole share in flight at once and the next
+// kernel's CTAs, which launch early under programmatic dependent launch and fit beside this one's small
+// CTAs, do the same while this kernel computes. Then activations are staged in consumption order, each
+// chunk runs through mma.sync (exact integer weights, fp32 accumulate, fp32 group-scale fold), warps reduce
+// through shared memory, cluster ranks through distributed shared memory, and rank 0 stores.
 // Status word: a kernel whose bounded wait gives up records an error code here instead of hanging the GPU;
 // the host reads it with lb_device_error().
 __device__ int g_device_status;
@@ -279,72 +278,39 @@ void clear_device_error() {
   cudaMemcpyToSymbol(g_device_status, &z, sizeof(int));
 }
 
-__host__ __device__ inline int oneshot_row_bytes(int nl) { return nl * 64 + 64; }   // +64: rows g, g+1 on other banks
-
-struct OneshotLayout {
-  int w, x, red, part, bar, total;
-};
-
-__host__ __device__ inline OneshotLayout oneshot_layout(int M, int nl, int nw, int nsplit, int mt) {
-  OneshotLayout L;
-  L.w = 0;
-  L.x = 16 * oneshot_row_bytes(nl);
-  L.red = L.x + ((M * gemv_x_row_words(nl) * 4 + 15) & ~15);
-  L.part = L.red + nw * mt * 512;
-  L.bar = L.part + (nsplit > 1 ? nsplit * mt * 512 : 0);
-  L.total = L.bar + 16;
-  return L;
-}
-
 template <int MT, int CPW, bool EARLY>
 __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
   const int NW = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int K = p.K, N = p.N, M = p.M;
-  const int KC = K >> 7, KG = K / p.G, cpg = p.G >> 7;
+  const int KC = K >> 7, KG = p.KG, cpg = p.cpg;
   const int split = blockIdx.y, nsplit = gridDim.y;
-  const int c_begin = (int)((int64_t)KC * split / nsplit);
-  const int c_end = (int)((int64_t)KC * (split + 1) / nsplit);
+  // K range of this cluster rank; the divisions only run when K is split
+  const int c_begin = nsplit == 1 ? 0 : KC * split / nsplit;
+  const int c_end = nsplit == 1 ? KC : KC * (split + 1) / nsplit;
   const int nl = c_end - c_begin;
-  const int max_nl = (KC + nsplit - 1) / nsplit;   // every rank of a cluster lays shared memory out alike
-  const OneshotLayout L = oneshot_layout(M, max_nl, NW, nsplit, MT);
-  const int rbytes = oneshot_row_bytes(max_nl);
   const int row_words = gemv_x_row_words(nl);
-  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + L.x);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
   const int n0 = blockIdx.x * 16;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    mbar_fence_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-  if (!EARLY) pdl_wait();
-
-  // weights: rows n0..n0+15 (tail rows re-read row N-1, never stored), chunks c_begin..c_end
-  if (warp == 0) {
-    if (lane == 0) mbar_arrive_expect_tx(bar, 16u * (uint32_t)nl * 64u);
-    __syncwarp();
-    if (lane < 16) {
-      const int row = min(n0 + lane, N - 1);
-      bulk_copy_g2s(smem + L.w + lane * rbytes,
-                    reinterpret_cast<const uint8_t*>(p.w) + (size_t)row * (K >> 1) + (size_t)c_begin * 64,
-                    (uint32_t)nl * 64, bar);
-    }
-  }
-  // scales of this warp's chunks for rows g and g + 8
-  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);
+  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1, never stored
+  const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * (K >> 5) + t;
+  const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * (K >> 5) + t;
   const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
   const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
   const int c_warp = c_begin + warp;
+
+  uint4 qa[CPW], qb[CPW];
   uint16_t ssa[CPW], ssb[CPW];
+  pdl_launch_dependents();
+  if (!EARLY) pdl_wait();
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
     if (c < c_end) {
       const int grp = cpg == 1 ? c : c / cpg;
+      qa[i] = ldg_stream(wa + 4 * c);
+      qb[i] = ldg_stream(wb + 4 * c);
       ssa[i] = ldg_u16(sa + grp);
       ssb[i] = ldg_u16(sb + grp);
     }
@@ -359,21 +325,10 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int m = 0; m < M; ++m)
       for (int pi = threadIdx.x; pi < pairs; pi += blockDim.x) {
         const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-        xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
+        sw[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
       }
   }
   __syncthreads();
-
-  // the weights have landed (bounded wait: a timeout is reported, the tile's output is then undefined)
-  {
-    uint32_t spins = 0;
-    while (!mbar_try_wait(bar, 0)) {
-      if (++spins == kSpinLimit) {
-        atomicExch(&g_device_status, kErrBarrierTimeout);
-        break;
-      }
-    }
-  }
 
   float acc[MT][4];
 #pragma unroll
@@ -383,16 +338,12 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   int xoff[MT];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
-  const uint8_t* wrow_a = smem + L.w + g * rbytes + t * 16;
-  const uint8_t* wrow_b = wrow_a + 8 * rbytes;
 
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
     if (c < c_end) {
       const int lc = c - c_begin;
-      const uint4 qa = *reinterpret_cast<const uint4*>(wrow_a + lc * 64);
-      const uint4 qb = *reinterpret_cast<const uint4*>(wrow_b + lc * 64);
       float d[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
@@ -400,11 +351,11 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
         for (int j = 0; j < 4; ++j) d[mt][j] = 0.f;
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
-        uint32_t w0 = (&qa.x)[qd], w1 = (&qb.x)[qd];
+        uint32_t w0 = (&qa[i].x)[qd], w1 = (&qb[i].x)[qd];
         uint4 xb[MT];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
-          xb[mt] = *reinterpret_cast<const uint4*>(xs + xoff[mt] + lc * 64 + qd * 16);
+          xb[mt] = *reinterpret_cast<const uint4*>(sw + xoff[mt] + lc * 64 + qd * 16);
         // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
         uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
 #pragma unroll
@@ -427,9 +378,10 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     }
   }
 
-  // reduce the warps' partial tiles through shared memory: red[warp][mt][i][lane]
+  // reduce the warps' partial tiles: red[warp][mt][i][lane] (the activation buffer is free again)
   constexpr int kTile = MT * 128;
-  float* red = reinterpret_cast<float*>(smem + L.red);
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(sw);
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -450,12 +402,13 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, cta_sum(e));
     return;
   }
-  // cluster split-K: each rank writes its partial tile into its slot of rank 0's buffer, a cluster barrier
-  // publishes the slots, rank 0 adds them in rank order (a first barrier is not needed: rank 0's slot area
-  // is used for nothing else)
+  // cluster split-K: each rank writes its partial tile into its slot of rank 0's buffer (after a cluster
+  // barrier: the buffer follows rank 0's reduction area), a second barrier publishes the slots, rank 0 adds
+  // them in rank order
   cg::cluster_group cluster = cg::this_cluster();
-  float* part = reinterpret_cast<float*>(smem + L.part);
+  float* part = red + NW * kTile;
   float* dst = cluster.map_shared_rank(part, 0) + split * kTile;
+  cluster.sync();
   for (int e = threadIdx.x; e < kTile; e += blockDim.x) dst[e] = cta_sum(e);
   cluster.sync();
   if (split == 0) {
@@ -501,7 +454,10 @@ static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c,
 
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw) {
   const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
-  return (size_t)oneshot_layout(M, max_nl, nw, nsplit, M <= 8 ? 1 : 2).total;
+  const int mt = M <= 8 ? 1 : 2;
+  const size_t x_bytes = (size_t)M * gemv_x_row_words(max_nl) * 4;
+  const size_t red_bytes = (size_t)(nw + (nsplit > 1 ? nsplit : 0)) * mt * 128 * 4;
+  return x_bytes > red_bytes ? x_bytes : red_bytes;
 }
 
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {

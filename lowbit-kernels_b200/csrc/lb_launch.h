@@ -19,6 +19,8 @@ struct GemvParams {
   int M, N, K, G;
   int flags;
   int wait_guard;  // always 1 (see pdl_wait_after_loads)
+  int KG;          // K / G, groups per row
+  int cpg;         // G / 128, 128-wide chunks per group (mma layout kernels)
 };
 
 struct GemvConfig {
