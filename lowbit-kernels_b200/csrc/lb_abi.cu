@@ -25,8 +25,8 @@ int ok() {
   return LB_OK;
 }
 
-constexpr int kNumOptions = 6;
-std::atomic<int> g_opt[kNumOptions] = {{1}, {0}, {0}, {0}, {0}, {0}};
+constexpr int kNumOptions = 7;
+std::atomic<int> g_opt[kNumOptions] = {{1}, {0}, {0}, {0}, {0}, {0}, {0}};
 
 int g_sm_count = 0;  // SMs of the current device (set by check_device)
 
@@ -118,25 +118,32 @@ lb::GemvConfig gemv_config(int M, int N, int K) {
 // tiles alone would not cover the SMs or a CTA's share would exceed ~32 KB of weights (long-K layers); the
 // range's chunks are spread over NW warps with at most CPW each (CPW * 8 registers of weights per thread).
 lb::OneshotConfig oneshot_config(int M, int N, int K) {
-  lb::OneshotConfig c{0, 0, 0, g_opt[LB_OPT_PDL].load()};
+  lb::OneshotConfig c{0, 0, 0, 0, g_opt[LB_OPT_PDL].load()};
   const int sms = g_sm_count > 0 ? g_sm_count : 148;
-  const int nt = (N + 15) / 16, kc = K >> 7;
+  const int kc = K >> 7;
+  // two row tiles per CTA while that still leaves about two CTAs per SM
+  int rt = (N + 31) / 32 >= 2 * sms ? 2 : 1;
+  const int forced_rt = g_opt[LB_OPT_GEMV_ROWTILES].load();
+  if (forced_rt == 1 || forced_rt == 2) rt = forced_rt;
+  const int nt = (N + 16 * rt - 1) / (16 * rt);
   int s = 1;
   while (s < 8 && s * 2 <= kc && ((kc + s - 1) / s > 32 || nt * s < sms)) ++s;
   const int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
   if (forced >= 1 && forced <= 8 && forced <= kc) s = forced;
   const int nl = (kc + s - 1) / s;
-  int nw = (nl + 3) / 4;
+  int nw = nl <= 16 ? (nl + 1) / 2 : (nl + 3) / 4;
   const int fw = g_opt[LB_OPT_GEMV_WARPS].load();
   if (fw >= 1 && fw <= 16) nw = fw;
   if (nw > 16) nw = 16;
   const int per = (nl + nw - 1) / nw;
-  const int cpw = per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 0;
+  int cpw = per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 0;
+  if (cpw == 8) rt = 1;
   if (cpw == 0) return c;
-  if (lb::oneshot_smem_bytes(M, K, s, nw) > 200 * 1024) return c;
+  if (lb::oneshot_smem_bytes(M, K, s, nw, rt) > 200 * 1024) return c;
   c.warps = nw;
   c.cpw = cpw;
   c.ksplit = s;
+  c.rt = rt;
   return c;
 }
 

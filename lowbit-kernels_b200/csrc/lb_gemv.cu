@@ -255,14 +255,20 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
   if (nsplit > 1) cg::this_cluster().sync();   // rank 0's buffers stay alive until every rank is done with them
 }
 
-// One-shot GEMV (M <= 16), the decode path. One CTA owns one 16-row tile and a K range (a cluster of S CTAs
-// splits long K); its warps split the range's chunks, at most CPW each. At entry every thread issues ALL of
-// its weight and scale loads (register destinations, L1 bypassed) -- before waiting on the previous kernel
-// when the weights are known static -- so each CTA has its whole share in flight at once and the next
-// kernel's CTAs, which launch early under programmatic dependent launch and fit beside this one's small
-// CTAs, do the same while this kernel computes. Then activations are staged in consumption order, each
-// chunk runs through mma.sync (exact integer weights, fp32 accumulate, fp32 group-scale fold), warps reduce
-// through shared memory, cluster ranks through distributed shared memory, and rank 0 stores.
+// One-shot GEMV (M <= 16), the decode path. One CTA owns RT 16-row tiles and a K range (a cluster of S
+// CTAs splits long K); its warps split the range's chunks, at most CPW each. At entry every thread issues
+// ALL of its weight and scale loads (register destinations, L1 bypassed) -- ahead of the wait on the previous
+// kernel when the weights are known static -- so the whole share is in flight at once while the previous
+// kernel finishes. The kernel is built to issue as few instructions as possible after that wait, because in
+// a chain of decode kernels that post-wait work is what sets the pace:
+//   * activations are staged with one 16-byte L2 load and four shared stores per eight values;
+//   * each warp runs two row tiles against the same activation fragments;
+//   * a weight fragment costs one LOP3: nibbles OR-ed into the fp16 mantissa of 1024 give 1024 + u (low
+//     nibble) or 1024 + 16u (high nibble) exactly, and go to the tensor core as they are. Low-form and
+//     high-form pairs use separate k16 steps and accumulators; one extra mma per step against a constant A of
+//     -1032 (low) or -1152 (= -72 * 16, high) cancels the bias, so D_low + D_high / 16 = sum (u - 8) x with
+//     exact products and fp32 sums, and the group scale is applied in fp32;
+//   * warps reduce through shared memory, cluster ranks through distributed shared memory, rank 0 stores.
 // Status word: a kernel whose bounded wait gives up records an error code here instead of hanging the GPU;
 // the host reads it with lb_device_error().
 __device__ int g_device_status;
@@ -278,7 +284,7 @@ void clear_device_error() {
   cudaMemcpyToSymbol(g_device_status, &z, sizeof(int));
 }
 
-template <int MT, int CPW, bool EARLY>
+template <int MT, int RT, int CPW, bool EARLY>
 __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
@@ -292,104 +298,144 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   const int c_end = nsplit == 1 ? KC : KC * (split + 1) / nsplit;
   const int nl = c_end - c_begin;
   const int row_words = gemv_x_row_words(nl);
-  const int n0 = blockIdx.x * 16;
-  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1, never stored
-  const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * (K >> 5) + t;
-  const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * (K >> 5) + t;
-  const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
-  const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+  const int n0 = blockIdx.x * (16 * RT);
   const int c_warp = c_begin + warp;
+  const size_t row_u4 = (size_t)(K >> 5);
 
-  uint4 qa[CPW], qb[CPW];
-  uint16_t ssa[CPW], ssb[CPW];
+  uint4 qa[RT][CPW], qb[RT][CPW];
+  uint16_t ssa[RT][CPW], ssb[RT][CPW];
   pdl_launch_dependents();
   if (!EARLY) pdl_wait();
 #pragma unroll
-  for (int i = 0; i < CPW; ++i) {
-    const int c = c_warp + NW * i;
-    if (c < c_end) {
-      const int grp = cpg == 1 ? c : c / cpg;
-      qa[i] = ldg_stream(wa + 4 * c);
-      qb[i] = ldg_stream(wb + 4 * c);
-      ssa[i] = ldg_u16(sa + grp);
-      ssb[i] = ldg_u16(sb + grp);
+  for (int r = 0; r < RT; ++r) {
+    const int ra = min(n0 + 16 * r + g, N - 1), rb = min(n0 + 16 * r + g + 8, N - 1);   // tail rows: row N-1
+    const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * row_u4 + t;
+    const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * row_u4 + t;
+    const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+#pragma unroll
+    for (int i = 0; i < CPW; ++i) {
+      const int c = c_warp + NW * i;
+      if (c < c_end) {
+        const int grp = cpg == 1 ? c : c / cpg;
+        qa[r][i] = ldg_stream(wa + 4 * c);
+        qb[r][i] = ldg_stream(wb + 4 * c);
+        ssa[r][i] = ldg_u16(sa + grp);
+        ssb[r][i] = ldg_u16(sb + grp);
+      }
     }
   }
   if (EARLY) pdl_wait_after_loads(p.wait_guard);
 
   // activations of this K range in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
-  // holds the pair x[m][128 c + 8 s + 2 t .. +1], s = 4 qd + e
+  // holds the pair x[m][128 c + 8 s + 2 t .. +1], s = 4 qd + e. Thread item i covers the 8 values
+  // k = 8 i .. 8 i + 7 of the range: one 16-byte load, four stores at a 4-word stride.
   {
-    const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x) + (size_t)c_begin * 64;
-    const int pairs = nl * 64;
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x) + (size_t)c_begin * 16;
+    const int items = nl * 16;
     for (int m = 0; m < M; ++m)
-      for (int pi = threadIdx.x; pi < pairs; pi += blockDim.x) {
-        const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-        sw[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
+      for (int it = threadIdx.x; it < items; it += blockDim.x) {
+        uint4 v;
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(xv + (size_t)m * (K >> 3) + it));
+        const int lc = it >> 4, sidx = it & 15;
+        uint32_t* d = sw + m * row_words + lc * 64 + (sidx >> 2) * 16 + (sidx & 3);
+        d[0] = v.x;
+        d[4] = v.y;
+        d[8] = v.z;
+        d[12] = v.w;
       }
   }
   __syncthreads();
 
-  float acc[MT][4];
+  float acc[RT][MT][4];
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+  for (int r = 0; r < RT; ++r)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[r][mt][i] = 0.f;
   int xoff[MT];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
+  constexpr uint32_t kNeg1032 = 0xE408E408u, kNeg1152 = 0xE480E480u;
 
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
     if (c < c_end) {
       const int lc = c - c_begin;
-      float d[MT][4];
+      float dl[RT][MT][4], dh[RT][MT][4], cl[MT][4], ch[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) d[mt][j] = 0.f;
+        for (int j = 0; j < 4; ++j) {
+          cl[mt][j] = 0.f;
+          ch[mt][j] = 0.f;
+#pragma unroll
+          for (int r = 0; r < RT; ++r) {
+            dl[r][mt][j] = 0.f;
+            dh[r][mt][j] = 0.f;
+          }
+        }
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
-        uint32_t w0 = (&qa[i].x)[qd], w1 = (&qb[i].x)[qd];
         uint4 xb[MT];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
           xb[mt] = *reinterpret_cast<const uint4*>(sw + xoff[mt] + lc * 64 + qd * 16);
-        // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
-        uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
+        // bias cancellation, shared by the row tiles: low step k = .. + 2t (pair 0) and .. + 16 + 2t (pair 2),
+        // high step k = .. + 8 + 2t (pair 1) and .. + 24 + 2t (pair 3)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
-        // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
-        w0 >>= 8;
-        w1 >>= 8;
-        f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+        for (int mt = 0; mt < MT; ++mt) {
+          mma16816(cl[mt], kNeg1032, kNeg1032, kNeg1032, kNeg1032, xb[mt].x, xb[mt].z);
+          mma16816(ch[mt], kNeg1152, kNeg1152, kNeg1152, kNeg1152, xb[mt].y, xb[mt].w);
+        }
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+        for (int r = 0; r < RT; ++r) {
+          const uint32_t w0 = (&qa[r][i].x)[qd], w1 = (&qb[r][i].x)[qd];
+          const uint32_t v0 = w0 >> 8, v1 = w1 >> 8;
+          const uint32_t l0 = (w0 & 0x000F000Fu) | kMagic, l1 = (w1 & 0x000F000Fu) | kMagic;
+          const uint32_t l2 = (v0 & 0x000F000Fu) | kMagic, l3 = (v1 & 0x000F000Fu) | kMagic;
+          const uint32_t h0 = (w0 & 0x00F000F0u) | kMagic, h1 = (w1 & 0x00F000F0u) | kMagic;
+          const uint32_t h2 = (v0 & 0x00F000F0u) | kMagic, h3 = (v1 & 0x00F000F0u) | kMagic;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            mma16816(dl[r][mt], l0, l1, l2, l3, xb[mt].x, xb[mt].z);
+            mma16816(dh[r][mt], h0, h1, h2, h3, xb[mt].y, xb[mt].w);
+          }
+        }
       }
-      const float s0 = h2f_bits(ssa[i]), s1 = h2f_bits(ssb[i]);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
-        acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
-        acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
-        acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
+      for (int r = 0; r < RT; ++r) {
+        const float s0 = h2f_bits(ssa[r][i]), s1 = h2f_bits(ssb[r][i]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float v = fmaf(dh[r][mt][j] + ch[mt][j], 0.0625f, dl[r][mt][j] + cl[mt][j]);
+            acc[r][mt][j] = fmaf(j < 2 ? s0 : s1, v, acc[r][mt][j]);
+          }
       }
     }
   }
 
-  // reduce the warps' partial tiles: red[warp][mt][i][lane] (the activation buffer is free again)
-  constexpr int kTile = MT * 128;
+  // reduce the warps' partial tiles through shared memory: red[warp][r][mt][i][lane]
+  constexpr int kTile = RT * MT * 128;
   __syncthreads();
   float* red = reinterpret_cast<float*>(sw);
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+  for (int r = 0; r < RT; ++r)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) red[warp * kTile + mt * 128 + i * 32 + lane] = acc[mt][i];
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[warp * kTile + (r * MT + mt) * 128 + i * 32 + lane] = acc[r][mt][i];
   __syncthreads();
   auto store = [&](int e, float v) {
-    const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-    const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+    const int rm = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+    const int r = rm / MT, mt = rm - r * MT;
+    const int row = n0 + 16 * r + (ln >> 2) + (i >= 2 ? 8 : 0);
     const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
     if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
   };
@@ -402,7 +448,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, cta_sum(e));
     return;
   }
-  // cluster split-K: each rank writes its partial tile into its slot of rank 0's buffer (after a cluster
+  // cluster split-K: each rank writes its partial tiles into its slot of rank 0's buffer (after a cluster
   // barrier: the buffer follows rank 0's reduction area), a second barrier publishes the slots, rank 0 adds
   // them in rank order
   cg::cluster_group cluster = cg::this_cluster();
@@ -420,16 +466,17 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   }
 }
 
-template <int MT, int CPW>
+template <int MT, int RT, int CPW>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
-  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, CPW, true> : gemv_oneshot_kernel<MT, CPW, false>;
-  const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps);
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true>
+                                            : gemv_oneshot_kernel<MT, RT, CPW, false>;
+  const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps, RT);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.N + 15) / 16, c.ksplit, 1);
+  cfg.gridDim = dim3((p.N + 16 * RT - 1) / (16 * RT), c.ksplit, 1);
   cfg.blockDim = dim3(c.warps * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -452,19 +499,20 @@ static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c,
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw) {
+size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt) {
   const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
   const int mt = M <= 8 ? 1 : 2;
   const size_t x_bytes = (size_t)M * gemv_x_row_words(max_nl) * 4;
-  const size_t red_bytes = (size_t)(nw + (nsplit > 1 ? nsplit : 0)) * mt * 128 * 4;
+  const size_t red_bytes = (size_t)(nw + (nsplit > 1 ? nsplit : 0)) * rt * mt * 128 * 4;
   return x_bytes > red_bytes ? x_bytes : red_bytes;
 }
 
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
   const int mt = p.M <= 8 ? 1 : 2;
-#define LB_ONESHOT(MT_, CPW_) \
-  if (mt == MT_ && c.cpw == CPW_) return launch_oneshot_t<MT_, CPW_>(p, c, st);
-  LB_ONESHOT(1, 2) LB_ONESHOT(1, 4) LB_ONESHOT(1, 8) LB_ONESHOT(2, 2) LB_ONESHOT(2, 4) LB_ONESHOT(2, 8)
+#define LB_ONESHOT(MT_, RT_, CPW_) \
+  if (mt == MT_ && c.rt == RT_ && c.cpw == CPW_) return launch_oneshot_t<MT_, RT_, CPW_>(p, c, st);
+  LB_ONESHOT(1, 1, 2) LB_ONESHOT(1, 1, 4) LB_ONESHOT(1, 1, 8) LB_ONESHOT(1, 2, 2) LB_ONESHOT(1, 2, 4)
+  LB_ONESHOT(2, 1, 2) LB_ONESHOT(2, 1, 4) LB_ONESHOT(2, 1, 8) LB_ONESHOT(2, 2, 2) LB_ONESHOT(2, 2, 4)
 #undef LB_ONESHOT
   return cudaErrorInvalidConfiguration;
 }

@@ -37,12 +37,13 @@ cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream
 // one-shot GEMV (M <= 16): one 16-row tile per CTA, all weight loads issued at entry
 struct OneshotConfig {
   int warps;   // warps per CTA (1..16)
-  int cpw;     // most chunks per warp: 2, 4 or 8
+  int cpw;     // most chunks per warp: 2, 4 or 8 (8 only with one row tile)
   int ksplit;  // CTAs per cluster splitting K (1..8)
+  int rt;      // 16-row tiles per CTA: 1 or 2
   int pdl;
 };
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
-size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw);
+size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt);
 
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
 int device_error();   // synchronizes

@@ -15,7 +15,7 @@ import torch
 
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblowbit_b200.so"
 LAYOUT_IDS = {"canonical": 0, "v3": 1, "mma": 2}
-OPTIONS = {"pdl": 0, "early_weights": 1, "gemv_ksplit": 2, "gemv_warps": 3, "gemv_depth": 4, "gemv_kernel": 5}
+OPTIONS = {"pdl": 0, "early_weights": 1, "gemv_ksplit": 2, "gemv_warps": 3, "gemv_depth": 4, "gemv_kernel": 5, "gemv_rowtiles": 6}
 
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
