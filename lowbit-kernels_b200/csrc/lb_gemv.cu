@@ -263,11 +263,9 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
 // a chain of decode kernels that post-wait work is what sets the pace:
 //   * activations are staged with one 16-byte L2 load and four shared stores per eight values;
 //   * each warp runs two row tiles against the same activation fragments;
-//   * a weight fragment costs one LOP3: nibbles OR-ed into the fp16 mantissa of 1024 give 1024 + u (low
-//     nibble) or 1024 + 16u (high nibble) exactly, and go to the tensor core as they are. Low-form and
-//     high-form pairs use separate k16 steps and accumulators; one extra mma per step against a constant A of
-//     -1032 (low) or -1152 (= -72 * 16, high) cancels the bias, so D_low + D_high / 16 = sum (u - 8) x with
-//     exact products and fp32 sums, and the group scale is applied in fp32;
+//   * nibbles become exact fp16 integers q = u - 8 in registers (mask-OR into the 1024.0 mantissa, one f16x2
+//     subtract or fma per pair) and feed mma.sync m16n8k16 as the A fragment: products q * x are exact, sums
+//     fp32, and each chunk's result is scaled by its group scale in fp32 (the weight is never rounded);
 //   * warps reduce through shared memory, cluster ranks through distributed shared memory, rank 0 stores.
 // Status word: a kernel whose bounded wait gives up records an error code here instead of hanging the GPU;
 // the host reads it with lb_device_error().
@@ -359,64 +357,49 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   int xoff[MT];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
-  constexpr uint32_t kNeg1032 = 0xE408E408u, kNeg1152 = 0xE480E480u;
-
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
     if (c < c_end) {
       const int lc = c - c_begin;
-      float dl[RT][MT][4], dh[RT][MT][4], cl[MT][4], ch[MT][4];
+      float d[RT][MT][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int r = 0; r < RT; ++r)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          cl[mt][j] = 0.f;
-          ch[mt][j] = 0.f;
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int r = 0; r < RT; ++r) {
-            dl[r][mt][j] = 0.f;
-            dh[r][mt][j] = 0.f;
-          }
-        }
+          for (int j = 0; j < 4; ++j) d[r][mt][j] = 0.f;
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
         uint4 xb[MT];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
           xb[mt] = *reinterpret_cast<const uint4*>(sw + xoff[mt] + lc * 64 + qd * 16);
-        // bias cancellation, shared by the row tiles: low step k = .. + 2t (pair 0) and .. + 16 + 2t (pair 2),
-        // high step k = .. + 8 + 2t (pair 1) and .. + 24 + 2t (pair 3)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          mma16816(cl[mt], kNeg1032, kNeg1032, kNeg1032, kNeg1032, xb[mt].x, xb[mt].z);
-          mma16816(ch[mt], kNeg1152, kNeg1152, kNeg1152, kNeg1152, xb[mt].y, xb[mt].w);
-        }
 #pragma unroll
         for (int r = 0; r < RT; ++r) {
-          const uint32_t w0 = (&qa[r][i].x)[qd], w1 = (&qb[r][i].x)[qd];
-          const uint32_t v0 = w0 >> 8, v1 = w1 >> 8;
-          const uint32_t l0 = (w0 & 0x000F000Fu) | kMagic, l1 = (w1 & 0x000F000Fu) | kMagic;
-          const uint32_t l2 = (v0 & 0x000F000Fu) | kMagic, l3 = (v1 & 0x000F000Fu) | kMagic;
-          const uint32_t h0 = (w0 & 0x00F000F0u) | kMagic, h1 = (w1 & 0x00F000F0u) | kMagic;
-          const uint32_t h2 = (v0 & 0x00F000F0u) | kMagic, h3 = (v1 & 0x00F000F0u) | kMagic;
+          uint32_t w0 = (&qa[r][i].x)[qd], w1 = (&qb[r][i].x)[qd];
+          // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
+          uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            mma16816(dl[r][mt], l0, l1, l2, l3, xb[mt].x, xb[mt].z);
-            mma16816(dh[r][mt], h0, h1, h2, h3, xb[mt].y, xb[mt].w);
-          }
+          for (int mt = 0; mt < MT; ++mt) mma16816(d[r][mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
+          // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
+          w0 >>= 8;
+          w1 >>= 8;
+          f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) mma16816(d[r][mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
         }
       }
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
         const float s0 = h2f_bits(ssa[r][i]), s1 = h2f_bits(ssb[r][i]);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float v = fmaf(dh[r][mt][j] + ch[mt][j], 0.0625f, dl[r][mt][j] + cl[mt][j]);
-            acc[r][mt][j] = fmaf(j < 2 ? s0 : s1, v, acc[r][mt][j]);
-          }
+        for (int mt = 0; mt < MT; ++mt) {
+          acc[r][mt][0] = fmaf(s0, d[r][mt][0], acc[r][mt][0]);
+          acc[r][mt][1] = fmaf(s0, d[r][mt][1], acc[r][mt][1]);
+          acc[r][mt][2] = fmaf(s1, d[r][mt][2], acc[r][mt][2]);
+          acc[r][mt][3] = fmaf(s1, d[r][mt][3], acc[r][mt][3]);
+        }
       }
     }
   }
