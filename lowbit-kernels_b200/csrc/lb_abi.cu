@@ -114,30 +114,34 @@ lb::GemvConfig gemv_config(int M, int N, int K) {
   return best;
 }
 
-// One-shot GEMV tiling: a CTA is one 16-row tile and a K range. K is split over a cluster of S CTAs when the
-// tiles alone would not cover the SMs or a CTA's share would exceed ~32 KB of weights (long-K layers); the
-// range's chunks are spread over NW warps with at most CPW each (CPW * 8 registers of weights per thread).
+// One-shot GEMV tiling, from a B200 sweep of the Qwen2.5 projections at M = 1 (every K-split 1..8, row tiles
+// 1..2, warps 2..16): splitting K across a cluster never paid (its two cluster barriers cost more than the
+// extra parallelism), one 16-row tile per CTA was best or within noise, and the post-wait critical path is
+// shortest with many warps per CTA -- 16 on layers up to 4096 rows, 8 on wider ones, never more than the
+// number of 128-wide chunks. A K split remains only where the staged activations would not fit otherwise.
 lb::OneshotConfig oneshot_config(int M, int N, int K) {
   lb::OneshotConfig c{0, 0, 0, 0, g_opt[LB_OPT_PDL].load()};
-  const int sms = g_sm_count > 0 ? g_sm_count : 148;
   const int kc = K >> 7;
-  // two row tiles per CTA while that still leaves about two CTAs per SM
-  int rt = (N + 31) / 32 >= 2 * sms ? 2 : 1;
+  int rt = 1;
   const int forced_rt = g_opt[LB_OPT_GEMV_ROWTILES].load();
   if (forced_rt == 1 || forced_rt == 2) rt = forced_rt;
-  const int nt = (N + 16 * rt - 1) / (16 * rt);
   int s = 1;
-  while (s < 8 && s * 2 <= kc && ((kc + s - 1) / s > 32 || nt * s < sms)) ++s;
   const int forced = g_opt[LB_OPT_GEMV_KSPLIT].load();
   if (forced >= 1 && forced <= 8 && forced <= kc) s = forced;
-  const int nl = (kc + s - 1) / s;
-  int nw = nl <= 16 ? (nl + 1) / 2 : (nl + 3) / 4;
+  int nl = (kc + s - 1) / s;
+  int nw = N >= 4096 ? 8 : 16;
   const int fw = g_opt[LB_OPT_GEMV_WARPS].load();
   if (fw >= 1 && fw <= 16) nw = fw;
-  if (nw > 16) nw = 16;
+  if (nw > nl) nw = nl;
+  // grow the split until every warp's share fits the register budget and the activations fit
+  while (!forced && s < 8 && s < kc &&
+         ((nl + nw - 1) / nw > (rt == 1 ? 8 : 4) || lb::oneshot_smem_bytes(M, K, s, nw, rt) > 200 * 1024)) {
+    ++s;
+    nl = (kc + s - 1) / s;
+    if (nw > nl) nw = nl;
+  }
   const int per = (nl + nw - 1) / nw;
-  int cpw = per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 0;
-  if (cpw == 8) rt = 1;
+  const int cpw = per <= 2 ? 2 : per <= 4 ? 4 : (per <= 8 && rt == 1) ? 8 : 0;
   if (cpw == 0) return c;
   if (lb::oneshot_smem_bytes(M, K, s, nw, rt) > 200 * 1024) return c;
   c.warps = nw;
