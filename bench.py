@@ -77,8 +77,9 @@ def measured_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if one exists."""
-    f = ROOT / "profiles" / "gemv_mma_m1_sweep.md"
+    """DRAM bytes (read + write) per launch of the GEMV over one sweep step, from the committed ncu summary
+    (profiles/gemv_oneshot_m1_sweep_dram.md), or None when no capture has been summarized."""
+    f = ROOT / "profiles" / "gemv_oneshot_m1_sweep_dram.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
@@ -367,8 +368,9 @@ def run_ours(args, rank, world, local):
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "gemv_mma_kernel<1,4,2> (M=1 decode GEMV)",
+            "bound": "hbm", "kernel": "gemv_oneshot_kernel (M=1 decode GEMV)",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "algorithmic_bytes_per_launch": round(step_bytes / launches_per_step),
             "frac": round(achieved / peak, 4), "peak_source": peak_src,
             "traffic": traffic,
             "note": "achieved = algorithmic bytes per launch / average launch duration over the timed region "
