@@ -325,26 +325,38 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   }
   if (EARLY) pdl_wait_after_loads(p.wait_guard);
 
-  // activations of this K range in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
-  // holds the pair x[m][128 c + 8 s + 2 t .. +1], s = 4 qd + e. Thread item i covers the 8 values
-  // k = 8 i .. 8 i + 7 of the range: one 16-byte load, four stores at a 4-word stride.
+  // Activations of this K range, copied verbatim (cp.async, L2 only) into shared memory rows of
+  // xrow_bytes = nl * 256 + 16 bytes (the 16-byte skew puts the 8 rows an ldmatrix reads on distinct banks).
+  // Within a k16 step the mma layout already follows natural k order, so ldmatrix on these rows yields the B
+  // fragments directly.
+  const int xrow_bytes = nl * 256 + 16;
   {
-    const uint4* xv = reinterpret_cast<const uint4*>(p.x) + (size_t)c_begin * 16;
-    const int items = nl * 16;
+    const uint8_t* xg = reinterpret_cast<const uint8_t*>(p.x) + (size_t)c_begin * 256;
+    const int pieces = nl * 16;   // 16-byte pieces per row
     for (int m = 0; m < M; ++m)
-      for (int it = threadIdx.x; it < items; it += blockDim.x) {
-        uint4 v;
-        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                     : "l"(xv + (size_t)m * (K >> 3) + it));
-        const int lc = it >> 4, sidx = it & 15;
-        uint32_t* d = sw + m * row_words + lc * 64 + (sidx >> 2) * 16 + (sidx & 3);
-        d[0] = v.x;
-        d[4] = v.y;
-        d[8] = v.z;
-        d[12] = v.w;
-      }
+      for (int it = threadIdx.x; it < pieces; it += blockDim.x)
+        cp_async16(smem_u32(smem + m * xrow_bytes + it * 16), xg + (size_t)m * (K * 2) + it * 16);
+    cp_async_commit();
   }
+
+  // the first chunk's fragments are decoded while the activations are in flight
+  uint32_t fr0[RT][4][8];
+  {
+    const int c = c_warp;
+    if (c < c_end) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          const uint32_t w0 = (&qa[r][0].x)[qd], w1 = (&qb[r][0].x)[qd];
+          fr0[r][qd][0] = q_pair_lo(w0); fr0[r][qd][1] = q_pair_lo(w1);
+          fr0[r][qd][2] = q_pair_hi(w0); fr0[r][qd][3] = q_pair_hi(w1);
+          fr0[r][qd][4] = q_pair_lo(w0 >> 8); fr0[r][qd][5] = q_pair_lo(w1 >> 8);
+          fr0[r][qd][6] = q_pair_hi(w0 >> 8); fr0[r][qd][7] = q_pair_hi(w1 >> 8);
+        }
+    }
+  }
+  cp_async_wait<0>();
   __syncthreads();
 
   float acc[RT][MT][4];
@@ -354,9 +366,13 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[r][mt][i] = 0.f;
-  int xoff[MT];
+  // ldmatrix row addresses: lane L serves row (L & 7) of 8x8 matrix L >> 3 (k offset 8 * (L >> 3) in a 32-k
+  // block); activation rows past M repeat row M - 1 (their outputs are dropped)
+  uint32_t xaddr[MT];
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
+  for (int mt = 0; mt < MT; ++mt)
+    xaddr[mt] = smem_u32(smem + min(8 * mt + (lane & 7), M - 1) * xrow_bytes + (lane >> 3) * 16);
+
 #pragma unroll
   for (int i = 0; i < CPW; ++i) {
     const int c = c_warp + NW * i;
@@ -371,23 +387,26 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
           for (int j = 0; j < 4; ++j) d[r][mt][j] = 0.f;
 #pragma unroll
       for (int qd = 0; qd < 4; ++qd) {
-        uint4 xb[MT];
+        uint32_t xb[MT][4];
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-          xb[mt] = *reinterpret_cast<const uint4*>(sw + xoff[mt] + lc * 64 + qd * 16);
+        for (int mt = 0; mt < MT; ++mt) ldsm_x4(xb[mt], xaddr[mt] + lc * 256 + qd * 64);
 #pragma unroll
         for (int r = 0; r < RT; ++r) {
-          uint32_t w0 = (&qa[r][i].x)[qd], w1 = (&qb[r][i].x)[qd];
-          // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
-          uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
+          uint32_t f[8];
+          if (i == 0) {
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma16816(d[r][mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
-          // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
-          w0 >>= 8;
-          w1 >>= 8;
-          f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
+            for (int j = 0; j < 8; ++j) f[j] = fr0[r][qd][j];
+          } else {
+            const uint32_t w0 = (&qa[r][i].x)[qd], w1 = (&qb[r][i].x)[qd];
+            f[0] = q_pair_lo(w0); f[1] = q_pair_lo(w1); f[2] = q_pair_hi(w0); f[3] = q_pair_hi(w1);
+            f[4] = q_pair_lo(w0 >> 8); f[5] = q_pair_lo(w1 >> 8); f[6] = q_pair_hi(w0 >> 8); f[7] = q_pair_hi(w1 >> 8);
+          }
+          // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t); step 2qd + 1: pairs 2 and 3
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) mma16816(d[r][mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
+          for (int mt = 0; mt < MT; ++mt) {
+            mma16816(d[r][mt], f[0], f[1], f[2], f[3], xb[mt][0], xb[mt][1]);
+            mma16816(d[r][mt], f[4], f[5], f[6], f[7], xb[mt][2], xb[mt][3]);
+          }
         }
       }
 #pragma unroll
@@ -485,7 +504,7 @@ static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c,
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt) {
   const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
   const int mt = M <= 8 ? 1 : 2;
-  const size_t x_bytes = (size_t)M * gemv_x_row_words(max_nl) * 4;
+  const size_t x_bytes = (size_t)M * (max_nl * 256 + 16);
   const size_t red_bytes = (size_t)(nw + (nsplit > 1 ? nsplit : 0)) * rt * mt * 128 * 4;
   return x_bytes > red_bytes ? x_bytes : red_bytes;
 }
