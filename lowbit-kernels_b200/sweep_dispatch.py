@@ -102,7 +102,8 @@ def derive(results, wide_n=3072):
             else:
                 break
         return best
-    gemv_rows = wins("v6_us", "v5_us", lambda r: True) or 1
+    # versions 6 and 5 run the same kernel up to 8 rows: ties go to version 6 up to its row limit
+    gemv_rows = max(wins("v6_us", "v5_us", lambda r: True), max(r["M"] for r in results if "v6_us" in r))
     v5_rows = wins("v5_us", "dequant_cublas_us", lambda r: True)
     v5_wide = wins("v5_us", "dequant_cublas_us", lambda r: r["N"] >= wide_n)
     return {"AUTO_GEMV_ROWS": max(1, gemv_rows), "AUTO_V5_ROWS": max(v5_rows, gemv_rows),
