@@ -51,7 +51,8 @@ typedef enum lb_option {
   LB_OPT_GEMV_KSPLIT = 2,   /* 0 (default): automatic; 1..8 forces the GEMV's K-split cluster size */
   LB_OPT_GEMV_WARPS = 3,    /* 0 (default): automatic; 4, 8 or 16 forces the GEMV's warps per CTA */
   LB_OPT_GEMV_DEPTH = 4,    /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
-  LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 forces the persistent copy-ring GEMV */
+  LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 forces the persistent copy-ring GEMV, 2 the tcgen05
+                               GEMM (any M <= 64) */
   LB_OPT_GEMV_ROWTILES = 6  /* 0 (default): automatic; 1 or 2 forces the one-shot GEMV's 16-row tiles per CTA */
 } lb_option;
 

@@ -157,6 +157,11 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
                    (int)(group / 128)};
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
+  if (kernel == 2 || (kernel == 0 && m > 16)) {
+    // tcgen05: one CTA per 128-row tile, tensor-memory accumulators
+    if (lb::gemm_tc05_smem_bytes((int)m, (int)k, (int)group) <= 227 * 1024)
+      return launched(lb::launch_gemm_tc05(p, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm_tc");
+  }
   if (kernel != 1 && m <= 16) {
     const lb::OneshotConfig c = oneshot_config((int)m, (int)n, (int)k);
     if (c.warps > 0) return launched(lb::launch_gemv_oneshot(p, c, st), "w4_gemv");
@@ -195,9 +200,15 @@ const char* lb_status_string(int status) {
 
 const char* lb_last_error(void) { return g_err; }
 
-int lb_device_error(void) { return lb::device_error(); }
+int lb_device_error(void) {
+  const int a = lb::device_error();
+  return a ? a : lb::gemm_tc_device_error();
+}
 
-void lb_clear_device_error(void) { lb::clear_device_error(); }
+void lb_clear_device_error(void) {
+  lb::clear_device_error();
+  lb::gemm_tc_clear_device_error();
+}
 
 int lb_set_option(int option, int value) {
   if (option < 0 || option >= kNumOptions) return -1;

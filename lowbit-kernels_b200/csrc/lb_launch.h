@@ -58,12 +58,10 @@ cudaError_t launch_quantize(const void* w, int w_is_half, uint8_t* packed, __hal
                             const float* clip, int n_clip, cudaStream_t st);
 cudaError_t launch_repack(const uint8_t* canonical, uint8_t* out, int N, int K, int layout, cudaStream_t st);
 
-// tensor-core skinny GEMM (lb_gemm_tc.cu)
-struct GemmConfig {
-  int n_tile;   // MMA N (activation rows, padded): 16, 32, 48 or 64
-  int ksplit;   // CTAs per cluster splitting K
-  int pdl;
-};
-cudaError_t launch_gemm_tc(const GemvParams& p, const GemmConfig& c, cudaStream_t st);
+// tcgen05 skinny GEMM (lb_gemm_tc.cu): 17 <= M <= 64, one CTA per 128-row tile
+cudaError_t launch_gemm_tc05(const GemvParams& p, bool pdl, cudaStream_t st);
+size_t gemm_tc05_smem_bytes(int M, int K, int G);
+int gemm_tc_device_error();   // synchronizes
+void gemm_tc_clear_device_error();
 
 }  // namespace lb

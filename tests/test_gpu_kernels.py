@@ -2,10 +2,12 @@
 
 Bars (from the reference's gates, bench/gpu_run.py:201-247, and the build's own contract):
   * dequantize, quantize and repack: bit-exact against the oracle / the golden model;
-  * GEMV and tensor-core GEMM: normalized error max|y - y64| / RMS(y64) <= 3e-3 against the fp64 oracle, and
-    every output within 1 fp16 ulp of the correctly rounded fp64 result (the kernels accumulate exact products
-    in fp32, so only the final rounding to fp16 remains), which is tighter than the reference kernels' own
-    error (fp16 partial sums);
+  * mma.sync GEMV / GEMM (up to 16 rows): normalized error max|y - y64| / RMS(y64) <= 3e-3 against the fp64
+    oracle, and every output within 1 fp16 ulp of the correctly rounded fp64 result (the kernels accumulate
+    exact products in fp32 per 128-wide chunk, so only the final rounding to fp16 remains), which is tighter
+    than the reference kernels' own error (fp16 partial sums);
+  * tcgen05 GEMM (17-64 rows): the same 3e-3 gate, and no worse than cuBLAS on the same fp16-dequantized
+    weights (check_gemm_output);
   * the overflow known answer exactly (bench/gpu_run.py:144-159).
 """
 import numpy as np
@@ -174,13 +176,50 @@ def test_both_gemv_kernels(layers, kernel, name, m):
     check_output(y, ref_y(x, packed, scales, 128), f"kernel {kernel} {name} M={m}")
 
 
+def check_gemm_output(y_gpu, y64, x16, packed, scales, group, what):
+    """The tcgen05 GEMM multiplies by fp16_rn(q * scale) -- the dequantized weights -- and accumulates a whole
+    row of K in the tensor core's fp32 accumulator, exactly the arithmetic of cuBLAS on dequantize()'s output
+    (the path it replaces). Bars: normalized error <= 3e-3 against fp64, and against the fp64 product with the
+    same fp16 weights, a max error at most 2x and a mean error at most 1.5x those of cuBLAS on the same inputs."""
+    y = y_gpu.double().cpu().numpy()
+    rms = np.sqrt(np.mean(y64 ** 2))
+    assert np.isfinite(y).all(), what
+    err = np.abs(y - y64).max() / rms
+    assert err <= NORM_BOUND, f"{what}: normalized error {err:.3e}"
+    w16 = O.c_dequantize_f16(packed, scales, group)
+    y16w = x16.double().numpy() @ w16.astype(np.float64).T
+    yc = torch.nn.functional.linear(x16.cuda(), torch.from_numpy(w16).cuda()).double().cpu().numpy()
+    e_ours, e_cublas = np.abs(y - y16w), np.abs(yc - y16w)
+    assert e_ours.max() <= 2 * e_cublas.max(), f"{what}: max error {e_ours.max():.3e} vs cuBLAS {e_cublas.max():.3e}"
+    assert e_ours.mean() <= 1.5 * e_cublas.mean(), \
+        f"{what}: mean error {e_ours.mean():.3e} vs cuBLAS {e_cublas.mean():.3e}"
+
+
+@pytest.mark.parametrize("name", [s[0] for s in SHAPES + EDGE])
+@pytest.mark.parametrize("m", [1, 17, 24, 32, 33, 48, 64])
+def test_tcgen05_gemm_parity(layers, name, m):
+    """The tcgen05 kernel at every NB (32 / 48 / 64), forced for M < 17 too."""
+    k, n, w, packed, scales, wq = layers[name]
+    x = x_for(m, k, k + n + 3 * m)
+    e = ops.ext()
+    prev = e.set_option("gemv_kernel", 2)
+    try:
+        y = ops.gemv(x.cuda(), wq, 5)
+    finally:
+        e.set_option("gemv_kernel", prev)
+    check_gemm_output(y, ref_y(x, packed, scales, 128), x, packed, scales, 128, f"tcgen05 {name} M={m}")
+
+
 @pytest.mark.parametrize("name", [s[0] for s in SHAPES + EDGE])
 @pytest.mark.parametrize("m", [1, 4, 12, 16, 33, 48, 64])
 def test_v5_gemm_parity(layers, name, m):
     k, n, w, packed, scales, wq = layers[name]
     x = x_for(m, k, k + n + m + 1)
     y = ops.gemv(x.cuda(), wq, 5)
-    check_output(y, ref_y(x, packed, scales, 128), f"v5 {name} M={m}")
+    if m > 16:
+        check_gemm_output(y, ref_y(x, packed, scales, 128), x, packed, scales, 128, f"v5 {name} M={m}")
+    else:
+        check_output(y, ref_y(x, packed, scales, 128), f"v5 {name} M={m}")
 
 
 @pytest.mark.parametrize("version", [1, 2, 3, 4])
