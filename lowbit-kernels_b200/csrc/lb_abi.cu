@@ -158,9 +158,10 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                    (int)(group / 128)};
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
   if (kernel == 2 || (kernel == 0 && m > 16)) {
-    // tcgen05: one CTA per 128-row tile, tensor-memory accumulators
-    if (lb::gemm_tc05_smem_bytes((int)m, (int)k, (int)group) <= 227 * 1024)
-      return launched(lb::launch_gemm_tc05(p, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm_tc");
+    // tcgen05: per 128-row tile a cluster of CTAs splitting K, tensor-memory accumulators
+    const int splits = lb::gemm_tc05_splits((int)m, (int)n, (int)k, (int)group, g_opt[LB_OPT_GEMV_KSPLIT].load());
+    if (splits > 0)
+      return launched(lb::launch_gemm_tc05(p, splits, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm_tc");
   }
   if (kernel != 1 && m <= 16) {
     const lb::OneshotConfig c = oneshot_config((int)m, (int)n, (int)k);

@@ -58,9 +58,11 @@ cudaError_t launch_quantize(const void* w, int w_is_half, uint8_t* packed, __hal
                             const float* clip, int n_clip, cudaStream_t st);
 cudaError_t launch_repack(const uint8_t* canonical, uint8_t* out, int N, int K, int layout, cudaStream_t st);
 
-// tcgen05 skinny GEMM (lb_gemm_tc.cu): 17 <= M <= 64, one CTA per 128-row tile
-cudaError_t launch_gemm_tc05(const GemvParams& p, bool pdl, cudaStream_t st);
-size_t gemm_tc05_smem_bytes(int M, int K, int G);
+// tcgen05 skinny GEMM (lb_gemm_tc.cu), M <= 64: per 128-row tile a cluster of `splits` CTAs splitting K.
+// gemm_tc05_splits picks the split for a shape on the current device (forced > 0: that split, capped by the
+// cluster limit and the number of K chunks), 0 if the shape does not fit the kernel.
+int gemm_tc05_splits(int M, int N, int K, int G, int forced);
+cudaError_t launch_gemm_tc05(const GemvParams& p, int splits, bool pdl, cudaStream_t st);
 int gemm_tc_device_error();   // synchronizes
 void gemm_tc_clear_device_error();
 

@@ -160,11 +160,12 @@ def test_v6_gemv_parity(layers, name, m):
     check_output(y, ref_y(x, packed, scales, 128), f"v6 {name} M={m}")
 
 
-@pytest.mark.parametrize("kernel", [1, 2])
+@pytest.mark.parametrize("kernel", [0, 1, 2])
 @pytest.mark.parametrize("name", ["0.5b.kv", "1.5b.up", "3b.down", "odd_n", "tiny", "k128"])
-@pytest.mark.parametrize("m", [1, 7, 16])
-def test_both_gemv_kernels(layers, kernel, name, m):
-    """The copy-ring GEMV (1) and the bulk-copy GEMV (2) each against the oracle, whatever the dispatch picks."""
+@pytest.mark.parametrize("m", [1, 7, 16, 24])
+def test_every_gemv_kernel(layers, kernel, name, m):
+    """Each kernel forced through the option against the oracle, whatever the dispatch would pick: automatic (0),
+    the copy-ring GEMV (1) and the tcgen05 GEMM (2)."""
     k, n, w, packed, scales, wq = layers[name]
     x = x_for(m, k, k + n + 5 * m)
     e = ops.ext()
@@ -173,7 +174,11 @@ def test_both_gemv_kernels(layers, kernel, name, m):
         y = ops.gemv(x.cuda(), wq, 6 if m <= 8 else 5)
     finally:
         e.set_option("gemv_kernel", prev)
-    check_output(y, ref_y(x, packed, scales, 128), f"kernel {kernel} {name} M={m}")
+    y64 = ref_y(x, packed, scales, 128)
+    if kernel == 2 or (kernel == 0 and m > 16):
+        check_gemm_output(y, y64, x, packed, scales, 128, f"kernel {kernel} {name} M={m}")
+    else:
+        check_output(y, y64, f"kernel {kernel} {name} M={m}")
 
 
 def check_gemm_output(y_gpu, y64, x16, packed, scales, group, what):
@@ -318,8 +323,9 @@ def test_cuda_graph_capture_and_pdl_options_give_identical_bits():
     e = ops.ext()
     wqs = [ops.W4Weight.from_float(torch.randn(n, k), layouts=("mma",)) for k, n in ((2048, 11008), (11008, 2048),
                                                                                        (896, 128))]
-    xs = [torch.randn(m, wq.k).half().cuda() for wq in wqs for m in (1, 16)]
-    pairs = [(x, wq) for x, wq in zip(xs, [w for w in wqs for _ in (1, 16)])]
+    rows = (1, 16, 40)   # one-shot GEMV, one-shot GEMM, tcgen05 GEMM
+    xs = [torch.randn(m, wq.k).half().cuda() for wq in wqs for m in rows]
+    pairs = [(x, wq) for x, wq in zip(xs, [w for w in wqs for _ in rows])]
     eager = [ops.linear(x, wq) for x, wq in pairs]
     prev = {k: e.get_option(k) for k in ("pdl", "early_weights")}
     try:
