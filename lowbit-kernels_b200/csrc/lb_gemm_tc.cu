@@ -4,19 +4,19 @@
 // are the 128-row A operand, the activation rows the N side of the MMA (NB = M rounded up to 32, 48 or 64).
 // Grid: one column of CTAs per 128-row tile of W; the S CTAs of a column form a thread-block cluster that splits
 // K into S contiguous ranges and adds its fp32 partial tiles through distributed shared memory (no workspace).
-//   * 8 producer warps: each owns a 16-row slice of the tile. Per 128-wide K chunk a lane takes the 16-byte
-//     words t of rows g and g+8 (the mma layout is the m16n8k16 A fragment), turns them into fp16 weights
-//     fp16_rn((u - 8) * scale) -- bit-identical to the dequantize kernel -- and writes them with stmatrix into
-//     the canonical no-swizzle K-major layout (8x8 core matrices of 16-byte rows: the fragment registers of a
-//     warp are exactly four core matrices). Each lane keeps 8 chunks of raw words in flight in a private
-//     cp.async ring; the CTA's scales are staged once.
-//   * one TMA warp: a single thread loads the activations of each chunk with two 2-D tensor copies (64 k x NB
+//   * weight loader warp: one thread copies each 128-wide K chunk of the tile's packed weights (128 rows x 64
+//     bytes, mma layout) with a 2-D tensor copy (64-byte swizzle) into a 12-deep stage ring.
+//   * activation loader warp: one thread copies the chunk's activations with two 2-D tensor copies (64 k x NB
 //     rows, 128-byte swizzle; rows >= M read as zeros) into a 4-deep stage ring.
-//   * one MMA warp: a single thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=NB, K=16) per k16
-//     step with the fp32 accumulator in tensor memory; tcgen05.commit releases the stages.
-//   * the producers read the accumulator with tcgen05.ld (each warp its 32-lane quarter of the tile) and store
-//     fp16, or, split across a cluster, park fp32 partials in shared memory that every CTA of the cluster sums
-//     for its share of the outputs in a fixed rank order (deterministic).
+//   * 8 dequantizing warps, two per 32-lane quarter of tensor memory, taking alternate chunks: each thread takes
+//     its row's 64 bytes, turns them into fp16 weights fp16_rn((u - 8) * scale) -- bit-identical to the
+//     dequantize kernel -- and stores the 64 packed columns into tensor memory with tcgen05.st: the A operand
+//     never passes through shared memory.
+//   * MMA warp: a single thread issues tcgen05.mma.cta_group::1.kind::f16 with A in tensor memory (M=128, N=NB,
+//     K=16 per instruction) and the fp32 accumulator in tensor memory; tcgen05.commit releases the stages.
+//   * the dequantizing warps read the accumulator with tcgen05.ld and store fp16, or, split across a cluster,
+//     park fp32 partials in shared memory that every CTA of the cluster sums for its share of the outputs in a
+//     fixed rank order (deterministic).
 // Stages are handed over through mbarriers; every wait is bounded and records a status code instead of hanging,
 // no copy is left in flight at exit, and tensor memory is released on every path.
 #include <cuda.h>
@@ -34,17 +34,17 @@ __device__ int g_tc_status;
 
 namespace {
 
-constexpr int kProducerWarps = 8;
+constexpr int kDequantWarps = 8;
 constexpr int kMmaWarp = 8;
-constexpr int kTmaWarp = 9;
-constexpr int kThreads = 10 * 32;
-constexpr int kAStages = 2;          // dequantized weight tiles the tensor core reads
-constexpr int kBStages = 4;          // activation tiles in flight
-constexpr int kRing = 8;             // chunks of raw packed weights in flight per producer lane
-constexpr int kRingLaneBytes = 32;   // per chunk: the lane's 16-byte words of rows g and g + 8
-constexpr int kAStepBytes = 16 * 2 * 128;      // one k16 step of the 128-row A tile: 16 row groups x 2 k halves
-constexpr int kAStageBytes = 8 * kAStepBytes;  // a 128-wide K chunk
-constexpr int kMaxSplits = 8;        // portable cluster size
+constexpr int kWLoadWarp = 9;
+constexpr int kXLoadWarp = 10;
+constexpr int kThreads = 11 * 32;
+constexpr int kWStages = 12;          // packed weight chunks in flight
+constexpr int kWStageBytes = 128 * 64;
+constexpr int kBStages = 4;           // activation chunks in flight
+constexpr int kTmemCols = 256;        // accumulator (<= 64 columns) + two A stages of 64 columns
+constexpr int kTmemA = 64;            // first column of A stage 0
+constexpr int kMaxSplits = 8;         // portable cluster size
 constexpr int kSmemLimit = 227 * 1024;
 
 // an activation stage: two 64-wide k halves of NB rows x 128 bytes (each half a whole number of 1024-byte
@@ -52,18 +52,17 @@ constexpr int kSmemLimit = 227 * 1024;
 __host__ __device__ inline int b_stage_bytes(int nb) { return nb * 256; }
 
 struct TcLayout {
-  int a, b, ring, scales, bars, tmem_slot, total;
+  int w, b, scales, bars, tmem_slot, total;
 };
 
 // offsets from the 1024-byte aligned start of dynamic shared memory; `ngroups` = scale groups per CTA
 __host__ __device__ inline TcLayout tc_layout(int nb, int ngroups) {
   TcLayout L;
-  L.a = 0;
-  L.b = kAStages * kAStageBytes;
-  L.ring = L.b + kBStages * b_stage_bytes(nb);
-  L.scales = L.ring + kRing * kProducerWarps * 32 * kRingLaneBytes;
+  L.w = 0;
+  L.b = kWStages * kWStageBytes;
+  L.scales = L.b + kBStages * b_stage_bytes(nb);
   L.bars = L.scales + ((128 * ngroups * 2 + 15) & ~15);
-  L.tmem_slot = L.bars + (2 * kAStages + 2 * kBStages + 1) * 8;
+  L.tmem_slot = L.bars + (2 * kWStages + 2 * kBStages + 2 * 2 + 1) * 8;
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -71,7 +70,6 @@ __host__ __device__ inline TcLayout tc_layout(int nb, int ngroups) {
 __host__ __device__ inline int tc_nb(int m) { return m <= 32 ? 32 : m <= 48 ? 48 : 64; }
 
 struct TcParams {
-  const void* w;  // packed uint8 [N, K / 2], mma layout
   const void* s;  // fp16 [N, K / G]
   __half* y;      // fp16 [M, N]
   int M, N, K, KG, cpg;
@@ -88,40 +86,30 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
-  asm volatile("stmatrix.sync.aligned.x4.m8n8.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
-               "r"(r2), "r"(r3)
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// UMMA shared-memory descriptor (sm_100 format: version 1 at bit 46, layout type at bits 61-63).
-// No swizzle, K-major: core matrices of 8 rows x 16 bytes; LBO = byte distance between the two k halves of a
-// k16 step, SBO = between consecutive 8-row groups.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor (sm_100 format: version 1 at bit 46), 128-byte swizzle, K-major: rows of 128
+// bytes (64 fp16 k), 8-row atoms of 1024 bytes (SBO); a k16 step inside the atom starts 32 bytes further (the
+// swizzle is applied to the computed addresses, atoms 1024-byte aligned); layout type 2 at bits 61-63
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 16;                  // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;        // SBO
   d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
   return d;
 }
-// 128-byte swizzle, K-major: rows of 128 bytes (64 fp16 k), 8-row atoms of 1024 bytes (SBO); a k16 step inside
-// the atom starts 32 bytes further (the swizzle is applied to the computed addresses, atoms 1024-byte aligned)
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  return smem_desc(addr, 16, 1024) | ((uint64_t)2 << 61);
-}
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T
+__device__ __forceinline__ void umma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -136,6 +124,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
+}
+
+// 32 consecutive columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
+      "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
+      "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 // 2-D tensor copy global -> this CTA's shared memory (coordinates: innermost first), completing on `bar`
@@ -172,41 +172,67 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// One loader thread: streams chunks 0..nc-1 of a stage ring, refilling a stage once its consumers released it,
+// then waits for its own last copies so that none is in flight when the CTA exits. Returns false if a wait gave up.
+template <typename Issue>
+__device__ __forceinline__ void run_loader(int nc, int stages, uint64_t* full, uint64_t* empty, uint32_t bytes,
+                                           Issue issue) {
+  int issued = 0;
+  for (int i = 0; i < nc; ++i) {
+    const int s = i % stages;
+    if (i >= stages && !wait_bounded(&empty[s], ((i / stages) - 1) & 1)) break;
+    mbar_arrive_expect_tx(&full[s], bytes);
+    issue(i, s);
+    issued = i + 1;
+  }
+  for (int i = issued > stages ? issued - stages : 0; i < issued; ++i) wait_bounded(&full[i % stages], (i / stages) & 1);
+}
+
 }  // namespace
 
 template <int NB>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc05_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                                const TcParams p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                     const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const TcLayout L = tc_layout(NB, p.ngroups);
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty_a = full_a + kAStages;
-  uint64_t* full_b = empty_a + kAStages;
+  uint64_t* full_w = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty_w = full_w + kWStages;
+  uint64_t* full_b = empty_w + kWStages;
   uint64_t* empty_b = full_b + kBStages;
-  uint64_t* done = empty_b + kBStages;
+  uint64_t* full_a = empty_b + kBStages;
+  uint64_t* empty_a = full_a + 2;
+  uint64_t* done = empty_a + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int N = p.N, M = p.M, cpg = p.cpg, S = p.splits;
+  const int N = p.N, M = p.M, S = p.splits;
   const int n0 = blockIdx.x * 128;
   const int KC = p.K >> 7;
   const int c_begin = (KC * (int)blockIdx.y) / S, nc = (KC * ((int)blockIdx.y + 1)) / S - c_begin;
-  constexpr int kTmemCols = NB <= 32 ? 32 : 64;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&full_a[s], kProducerWarps * 32);
-      mbar_init(&empty_a[s], 1);
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&full_w[s], 1);
+      mbar_init(&empty_w[s], 4);   // the four warps of the chunk's parity
     }
     for (int s = 0; s < kBStages; ++s) {
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_b[s], 1);
     }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full_a[s], 4 * 32);
+      mbar_init(&empty_a[s], 1);
+    }
     mbar_init(done, 1);
     mbar_fence_init();
   }
-  if (warp == kTmaWarp && lane == 0)
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
   if (warp == kMmaWarp) {   // the MMA warp owns the tensor-memory allocation
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                  "r"(kTmemCols)
@@ -225,20 +251,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc05_kernel(const __grid_con
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     bool ok = true;
     for (int i = 0; i < nc; ++i) {
-      const int sa = i % kAStages, sb = i % kBStages;
-      if (ok) ok = wait_bounded(&full_a[sa], (i / kAStages) & 1);
+      const int sa = i & 1, sb = i % kBStages;
+      if (ok) ok = wait_bounded(&full_a[sa], (i >> 1) & 1);
       if (ok) ok = wait_bounded(&full_b[sb], (i / kBStages) & 1);
       tc_fence_after();
       if (lane == 0 && ok) {
-        const uint32_t a0 = smem_addr(smem + L.a + sa * kAStageBytes);
+        const uint32_t a0 = tmem + kTmemA + 64 * sa;
         const uint32_t b0 = smem_addr(smem + L.b + sb * b_stage_bytes(NB));
 #pragma unroll
         for (int st = 0; st < 8; ++st)
-          umma_f16(tmem, smem_desc(a0 + st * kAStepBytes, 128, 256),
-                   smem_desc_sw128(b0 + (st >> 2) * (NB * 128) + (st & 3) * 32), idesc, (i > 0 || st > 0) ? 1u : 0u);
+          umma_ts_f16(tmem, a0 + 8 * st, smem_desc_sw128(b0 + (st >> 2) * (NB * 128) + (st & 3) * 32), idesc,
+                      (i > 0 || st > 0) ? 1u : 0u);
       }
       __syncwarp();
-      if (lane == 0) {   // each arrives when this chunk's MMAs have read their stage
+      if (lane == 0) {   // each arrives when this chunk's MMAs have read their operands
         umma_commit(&empty_a[sa]);
         umma_commit(&empty_b[sb]);
       }
@@ -247,118 +273,105 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc05_kernel(const __grid_con
     if (lane == 0) umma_commit(done);
     __syncwarp();
     if (ok) wait_bounded(done, 0);   // no MMA in flight past this point
-  } else if (warp == kTmaWarp) {
-    // ------------------------------------------------------------------ activation loads
+  } else if (warp == kWLoadWarp) {
+    // ------------------------------------------------------------------ packed weights
     if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+      // static weights may be fetched before the stream dependency resolves (kFlagEarlyWeights)
+      if (!(p.flags & kFlagEarlyWeights) && p.wait_guard) pdl_wait();
+      run_loader(nc, kWStages, full_w, empty_w, kWStageBytes, [&](int i, int s) {
+        tma_load_2d(smem + L.w + s * kWStageBytes, &wmap, (c_begin + i) * 64, n0, &full_w[s]);
+      });
+    }
+    __syncwarp();
+  } else if (warp == kXLoadWarp) {
+    // ------------------------------------------------------------------ activations
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       if (p.wait_guard) pdl_wait();   // the activations come from the previous kernel in the stream
-      bool ok = true;
-      int issued = 0;
-      for (int i = 0; i < nc && ok; ++i) {
-        const int sb = i % kBStages;
-        if (i >= kBStages) ok = wait_bounded(&empty_b[sb], ((i / kBStages) - 1) & 1);
-        if (!ok) break;
-        uint8_t* dst = smem + L.b + sb * b_stage_bytes(NB);
-        const int kx = (c_begin + i) * 128;
-        mbar_arrive_expect_tx(&full_b[sb], b_stage_bytes(NB));
-        tma_load_2d(dst, &xmap, kx, 0, &full_b[sb]);
-        tma_load_2d(dst + NB * 128, &xmap, kx + 64, 0, &full_b[sb]);
-        issued = i + 1;
-      }
-      // no copy may outlive the CTA: wait for the last stages' transfers (already consumed phases pass at once)
-      for (int i = issued > kBStages ? issued - kBStages : 0; i < issued; ++i)
-        wait_bounded(&full_b[i % kBStages], (i / kBStages) & 1);
+      run_loader(nc, kBStages, full_b, empty_b, b_stage_bytes(NB), [&](int i, int s) {
+        uint8_t* dst = smem + L.b + s * b_stage_bytes(NB);
+        tma_load_2d(dst, &xmap, (c_begin + i) * 128, 0, &full_b[s]);
+        tma_load_2d(dst + NB * 128, &xmap, (c_begin + i) * 128 + 64, 0, &full_b[s]);
+      });
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------------ weight producers
-    const int g = lane >> 2, t = lane & 3;
-    const int pt = threadIdx.x;   // producer thread 0..255
-    const int ra = min(n0 + 16 * warp + g, N - 1), rb = min(n0 + 16 * warp + g + 8, N - 1);  // tail rows: N-1
-    const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * (p.K >> 5) + t;
-    const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * (p.K >> 5) + t;
-    // this lane's private ring of raw packed words: slot i % kRing holds (row g, row g + 8) of chunk i
-    const uint32_t ring = smem_addr(smem + L.ring) + (uint32_t)pt * (kRing * kRingLaneBytes);
-    auto issue = [&](int i) {
-      if (i < nc) {
-        const int c = c_begin + i;
-        cp_async_cg16(ring + (i % kRing) * kRingLaneBytes, wa + 4 * c);
-        cp_async_cg16(ring + (i % kRing) * kRingLaneBytes + 16, wb + 4 * c);
-      }
-      cp_async_group_commit();
-    };
-    // weights and scales may be fetched before the stream dependency resolves only when the caller declared
-    // them static (kFlagEarlyWeights); otherwise wait first
+    // ------------------------------------------------------------------ dequantizing warps
+    const int quarter = warp & 3, par = warp >> 2;   // TMEM lanes 32q.. ; chunks i = par, par + 2, ...
+    const int row = 32 * quarter + lane;             // row of the tile = TMEM lane
+    const int cpg = p.cpg;
     if (!(p.flags & kFlagEarlyWeights) && p.wait_guard) pdl_wait();
-#pragma unroll
-    for (int i = 0; i < kRing - 1; ++i) issue(i);
-    // scales of the CTA's groups, rows n0 .. n0 + 127 (tail rows repeat row N - 1): two threads per row
+    // scales of the CTA's groups, rows n0 .. n0 + 127 (tail rows repeat row N - 1)
     const int g0 = c_begin / cpg, ng = (c_begin + nc - 1) / cpg - g0 + 1;
     uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L.scales);
     {
-      const int r = pt >> 1;
-      const uint16_t* srow = reinterpret_cast<const uint16_t*>(p.s) + (size_t)min(n0 + r, N - 1) * p.KG + g0;
-      for (int gi = pt & 1; gi < ng; gi += 2) sc[r * p.ngroups + gi] = ldg_u16(srow + gi);
+      const uint16_t* srow = reinterpret_cast<const uint16_t*>(p.s) + (size_t)min(n0 + row, N - 1) * p.KG + g0;
+      for (int gi = par; gi < ng; gi += 2) sc[row * p.ngroups + gi] = ldg_u16(srow + gi);
     }
-    named_barrier(1, kProducerWarps * 32);
+    named_barrier(1, kDequantWarps * 32);
     if (p.wait_guard) pdl_wait();   // the outputs are written in stream order
-    // stmatrix row addresses: lane L writes row (L & 7) of core matrix j = L >> 3, which is row group
-    // 2 * warp + (j & 1) and k half j >> 1 of every k16 step
-    const int jm = lane >> 3;
-    const uint32_t a_row = (uint32_t)((((2 * warp + (jm & 1)) * 2 + (jm >> 1)) * 128) + (lane & 7) * 16);
-    const int sra = (16 * warp + g) * p.ngroups, srb = (16 * warp + g + 8) * p.ngroups;
+    // the row's 64 bytes sit at row * 64 in a weight stage, 16-byte word t at slot t ^ ((row >> 1) & 3)
+    const uint32_t wrow = smem_addr(smem + L.w) + (uint32_t)row * 64;
+    const uint32_t wsw = (uint32_t)(row >> 1) & 3u;
+    const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
     bool ok = true;
-    for (int i = 0; i < nc; ++i) {
-      const int sa = i % kAStages;
-      issue(i + kRing - 1);
-      cp_async_group_wait<kRing - 1>();   // this lane's copies of chunk i have landed (groups complete in order)
-      const uint8_t* slot = smem + L.ring + pt * (kRing * kRingLaneBytes) + (i % kRing) * kRingLaneBytes;
-      const uint4 qa = *reinterpret_cast<const uint4*>(slot);
-      const uint4 qb = *reinterpret_cast<const uint4*>(slot + 16);
-      const int grp = cpg == 1 ? i : (c_begin + i) / cpg - g0;
-      const uint32_t s2a = (uint32_t)sc[sra + grp] * 0x10001u, s2b = (uint32_t)sc[srb + grp] * 0x10001u;
-      if (i >= kAStages && ok) ok = wait_bounded(&empty_a[sa], ((i / kAStages) - 1) & 1);
-      __syncwarp();   // stmatrix is warp-collective
-      tc_fence_after();
-      // fp16_rn((u - 8) * scale), four core matrices per k16 step
-      const uint32_t abase = smem_addr(smem + L.a + sa * kAStageBytes) + a_row;
+    for (int i = par; i < nc; i += 2) {
+      const int sw = i % kWStages, sa = i & 1;
+      if (ok) ok = wait_bounded(&full_w[sw], (i / kWStages) & 1);
+      uint4 q[4];
 #pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
-        const uint32_t w0 = (&qa.x)[qd], w1 = (&qb.x)[qd];
-        // k16 step 2qd: pairs 0 and 1; step 2qd + 1: pairs 2 and 3
-        stsm_x4(abase + (2 * qd) * kAStepBytes, hmul2_bits(q_pair_lo(w0), s2a), hmul2_bits(q_pair_lo(w1), s2b),
-                hmul2_bits(q_pair_hi(w0), s2a), hmul2_bits(q_pair_hi(w1), s2b));
-        stsm_x4(abase + (2 * qd + 1) * kAStepBytes, hmul2_bits(q_pair_lo(w0 >> 8), s2a),
-                hmul2_bits(q_pair_lo(w1 >> 8), s2b), hmul2_bits(q_pair_hi(w0 >> 8), s2a),
-                hmul2_bits(q_pair_hi(w1 >> 8), s2b));
+      for (int t = 0; t < 4; ++t) q[t] = lds128(wrow + sw * kWStageBytes + ((t ^ wsw) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_w[sw]);
+      const int grp = (cpg == 1 ? c_begin + i : (c_begin + i) / cpg) - g0;
+      const uint32_t s2 = (uint32_t)sc[row * p.ngroups + grp] * 0x10001u;
+      if (i >= 2 && ok) ok = wait_bounded(&empty_a[sa], ((i >> 1) - 1) & 1);
+      __syncwarp();   // tcgen05.st is warp-collective
+      tc_fence_after();
+      // u32 qd of word t holds the pairs of columns 16qd + t (+4, +8, +12): column j = fp16 weights k 2j, 2j + 1
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t v[32];
+#pragma unroll
+        for (int d = 0; d < 2; ++d) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t w = (&q[t].x)[2 * hh + d];
+            v[16 * d + t] = hmul2_bits(q_pair_lo(w), s2);
+            v[16 * d + 4 + t] = hmul2_bits(q_pair_hi(w), s2);
+            v[16 * d + 8 + t] = hmul2_bits(q_pair_lo(w >> 8), s2);
+            v[16 * d + 12 + t] = hmul2_bits(q_pair_hi(w >> 8), s2);
+          }
+        }
+        tmem_st32(tmem + tlane + kTmemA + 64 * sa + 32 * hh, v);
       }
-      fence_async_smem();   // generic-proxy writes (stmatrix) become visible to the tensor core
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
       mbar_arrive(&full_a[sa]);
     }
-    cp_async_group_wait<0>();   // no ring copy is left in flight
     // epilogue: wait for the last MMA, then each warp reads its 32 lanes (rows) of the accumulator; warps q and
     // q + 4 share lanes 32q.. and alternate 16-column blocks
     if (ok) ok = wait_bounded(done, 0);
     __syncwarp();   // tcgen05.ld is warp-collective
     tc_fence_after();
-    const int quarter = warp & 3, half = warp >> 2;
-    const int trow = 32 * quarter + lane;   // row within the tile
-    float* red = reinterpret_cast<float*>(smem + L.a);   // [m][128] fp32 partials (the A stages are free now)
+    float* red = reinterpret_cast<float*>(smem + L.w);   // [m][128] fp32 partials (the weight ring is idle now)
 #pragma unroll
-    for (int blk = half; blk < NB / 16; blk += 2) {
+    for (int blk = par; blk < NB / 16; blk += 2) {
       const int col0 = blk * 16;
       uint32_t v[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col0, v);
+      tmem_ld16(tmem + tlane + (uint32_t)col0, v);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       if (S == 1) {
-        if (n0 + trow < N) {
+        if (n0 + row < N) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (col0 + j < M) p.y[(size_t)(col0 + j) * N + n0 + trow] = __float2half_rn(__uint_as_float(v[j]));
+            if (col0 + j < M) p.y[(size_t)(col0 + j) * N + n0 + row] = __float2half_rn(__uint_as_float(v[j]));
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (col0 + j < M) red[(col0 + j) * 128 + trow] = __uint_as_float(v[j]);
+          if (col0 + j < M) red[(col0 + j) * 128 + row] = __uint_as_float(v[j]);
       }
     }
   }
@@ -369,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc05_kernel(const __grid_con
     cluster_sync_all();
     const int e4 = 32 * M, r = (int)cluster_rank();
     const int e_begin = (e4 * r) / S, e_end = (e4 * (r + 1)) / S;
-    const uint32_t red0 = smem_addr(smem + L.a);
+    const uint32_t red0 = smem_addr(smem + L.w);
     for (int e = e_begin + (int)threadIdx.x; e < e_end; e += kThreads) {
       const int m = e >> 5, row4 = (e & 31) * 4;
       const uint32_t off = red0 + (uint32_t)(m * 128 + row4) * 4u;
@@ -425,7 +438,6 @@ int device_sms(int dev) {
   return v;
 }
 
-template <int NB>
 cudaLaunchConfig_t tc_config(int N, int splits, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + 127) / 128, splits, 1);
@@ -471,7 +483,7 @@ int max_active_clusters(int dev, int S, size_t smem) {
     auto kern = gemm_tc05_kernel<NB>;
     int n = 0;
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = tc_config<NB>(128 * S, S, smem, nullptr, attr, false);
+    cudaLaunchConfig_t cfg = tc_config(128 * S, S, smem, nullptr, attr, false);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess ||
         cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
       n = 0;
@@ -507,24 +519,36 @@ cudaError_t launch_tc_t(const GemvParams& g, int S, bool pdl, cudaStream_t st) {
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
   const int KC = g.K / 128;
-  TcParams p{g.w, g.s, g.y, g.M, g.N, g.K, g.KG, g.cpg, g.flags, g.wait_guard, S, groups_per_cta(KC, g.cpg, S)};
-  // activations as a [M, K] fp16 tensor; boxes of 64 k x NB rows, rows past M are filled with zeros
-  CUtensorMap xmap;
-  const cuuint64_t dims[2] = {(cuuint64_t)g.K, (cuuint64_t)g.M};
-  const cuuint64_t strides[1] = {(cuuint64_t)g.K * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)NB};
+  TcParams p{g.s, g.y, g.M, g.N, g.K, g.KG, g.cpg, g.flags, g.wait_guard, S, groups_per_cta(KC, g.cpg, S)};
   const cuuint32_t estride[2] = {1, 1};
-  if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(g.x), dims, strides, box, estride,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
+  // activations as a [M, K] fp16 tensor; boxes of 64 k x NB rows, rows past M are filled with zeros
+  CUtensorMap xmap, wmap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)g.K, (cuuint64_t)g.M};
+    const cuuint64_t strides[1] = {(cuuint64_t)g.K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)NB};
+    if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(g.x), dims, strides, box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  // packed weights as a [N, K / 2] byte tensor; boxes of one 64-byte chunk x 128 rows, rows past N read as zeros
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)g.K / 2, (cuuint64_t)g.N};
+    const cuuint64_t strides[1] = {(cuuint64_t)g.K / 2};
+    const cuuint32_t box[2] = {64, 128};
+    if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g.w), dims, strides, box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   const size_t smem = (size_t)tc_layout(NB, p.ngroups).total + 1024;
   auto kern = gemm_tc05_kernel<NB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = tc_config<NB>(g.N, S, smem, st, attr, pdl);
-  return cudaLaunchKernelEx(&cfg, kern, xmap, p);
+  cudaLaunchConfig_t cfg = tc_config(g.N, S, smem, st, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, kern, xmap, wmap, p);
 }
 
 }  // namespace
