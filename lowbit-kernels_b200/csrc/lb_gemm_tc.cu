@@ -5,15 +5,18 @@
 // Grid: one column of CTAs per 128-row tile of W; the S CTAs of a column form a thread-block cluster that splits
 // K into S contiguous ranges and adds its fp32 partial tiles through distributed shared memory (no workspace).
 //   * weight loader warp: one thread copies each 128-wide K chunk of the tile's packed weights (128 rows x 64
-//     bytes, mma layout) with a 2-D tensor copy (64-byte swizzle) into a 12-deep stage ring.
+//     bytes, mma layout) with a 2-D tensor copy (64-byte swizzle) into an 8-deep stage ring.
 //   * activation loader warp: one thread copies the chunk's activations with two 2-D tensor copies (64 k x NB
-//     rows, 128-byte swizzle; rows >= M read as zeros) into a 4-deep stage ring.
-//   * 8 dequantizing warps, two per 32-lane quarter of tensor memory, taking alternate chunks: each thread takes
-//     its row's 64 bytes, turns them into fp16 weights fp16_rn((u - 8) * scale) -- bit-identical to the
-//     dequantize kernel -- and stores the 64 packed columns into tensor memory with tcgen05.st: the A operand
-//     never passes through shared memory.
+//     rows, 128-byte swizzle; rows >= M read as zeros) into a 6-deep stage ring.
+//   * 8 dequantizing warps, two per 32-lane quarter of tensor memory, each taking one 64-wide K half of every
+//     chunk: a thread takes its row's 32 bytes of that half, turns them into fp16 weights
+//     fp16_rn((u - 8) * scale) -- bit-identical to the dequantize kernel -- and stores the 32 packed columns
+//     into tensor memory with tcgen05.st (3 stages): the A operand never passes through shared memory.
 //   * MMA warp: a single thread issues tcgen05.mma.cta_group::1.kind::f16 with A in tensor memory (M=128, N=NB,
-//     K=16 per instruction) and the fp32 accumulator in tensor memory; tcgen05.commit releases the stages.
+//     K=16 per instruction) and the fp32 accumulator in tensor memory. One tcgen05.commit per chunk (to a ring of
+//     completion barriers) releases both the activation stage and the tensor-memory stage; the next chunk's
+//     barriers are polled while this chunk's MMAs run, so the tensor core is fed back to back (one 128 x N x 16
+//     MMA costs about 100 cycles for any N <= 128 on B200: this, not memory, bounds the kernel at small M).
 //   * the dequantizing warps read the accumulator with tcgen05.ld and store fp16, or, split across a cluster,
 //     park fp32 partials in shared memory that every CTA of the cluster sums for its share of the outputs in a
 //     fixed rank order (deterministic).
@@ -39,10 +42,11 @@ constexpr int kMmaWarp = 8;
 constexpr int kWLoadWarp = 9;
 constexpr int kXLoadWarp = 10;
 constexpr int kThreads = 11 * 32;
-constexpr int kWStages = 12;          // packed weight chunks in flight
+constexpr int kWStages = 8;           // packed weight chunks in flight
 constexpr int kWStageBytes = 128 * 64;
-constexpr int kBStages = 4;           // activation chunks in flight
-constexpr int kTmemCols = 256;        // accumulator (<= 64 columns) + two A stages of 64 columns
+constexpr int kBStages = 6;           // activation chunks in flight
+constexpr int kAStages = 3;           // dequantized chunks in tensor memory
+constexpr int kTmemCols = 256;        // accumulator (<= 64 columns) + three A stages of 64 columns
 constexpr int kTmemA = 64;            // first column of A stage 0
 constexpr int kMaxSplits = 8;         // portable cluster size
 constexpr int kSmemLimit = 227 * 1024;
@@ -62,7 +66,7 @@ __host__ __device__ inline TcLayout tc_layout(int nb, int ngroups) {
   L.b = kWStages * kWStageBytes;
   L.scales = L.b + kBStages * b_stage_bytes(nb);
   L.bars = L.scales + ((128 * ngroups * 2 + 15) & ~15);
-  L.tmem_slot = L.bars + (2 * kWStages + 2 * kBStages + 2 * 2 + 1) * 8;
+  L.tmem_slot = L.bars + (2 * kWStages + 2 * kBStages + kAStages + 1) * 8;
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -82,6 +86,18 @@ struct TcParams {
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
+  atomicExch(&g_tc_status, kErrBarrierTimeout);
+  return false;
+}
+
+// both phases, polled together (each poll of a completed barrier still costs a full shared-memory round trip)
+__device__ __forceinline__ bool wait_pair(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb) {
+  bool da = false, db = false;
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (!da) da = mbar_try_wait(a, pa);
+    if (!db) db = mbar_try_wait(b, pb);
+    if (da && db) return true;
+  }
   atomicExch(&g_tc_status, kErrBarrierTimeout);
   return false;
 }
@@ -172,9 +188,9 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
 }
 
@@ -207,9 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_w = full_w + kWStages;
   uint64_t* full_b = empty_w + kWStages;
   uint64_t* empty_b = full_b + kBStages;
-  uint64_t* full_a = empty_b + kBStages;
-  uint64_t* empty_a = full_a + 2;
-  uint64_t* done = empty_a + 2;
+  uint64_t* full_a = empty_b + kBStages;       // dequantized chunk in tensor memory
+  uint64_t* done = full_a + kAStages;          // all MMAs complete
+  uint64_t* mma_done = empty_b;                // chunk i's MMAs complete: ring of kBStages (= empty_b)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = p.N, M = p.M, S = p.splits;
@@ -220,16 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&full_w[s], 1);
-      mbar_init(&empty_w[s], 4);   // the four warps of the chunk's parity
+      mbar_init(&empty_w[s], kDequantWarps);
     }
     for (int s = 0; s < kBStages; ++s) {
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_b[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&full_a[s], 4 * 32);
-      mbar_init(&empty_a[s], 1);
-    }
+    for (int s = 0; s < kAStages; ++s) mbar_init(&full_a[s], kDequantWarps * 32);
     mbar_init(done, 1);
     mbar_fence_init();
   }
@@ -246,33 +259,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
-    // instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, N = NB, M = 128
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-    bool ok = true;
-    for (int i = 0; i < nc; ++i) {
-      const int sa = i & 1, sb = i % kBStages;
-      if (ok) ok = wait_bounded(&full_a[sa], (i >> 1) & 1);
-      if (ok) ok = wait_bounded(&full_b[sb], (i / kBStages) & 1);
-      tc_fence_after();
-      if (lane == 0 && ok) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      // instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, N = NB, M = 128
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      bool ok = nc == 0 || wait_pair(&full_a[0], 0, &full_b[0], 0);
+      for (int i = 0; i < nc && ok; ++i) {
+        const int sa = i % kAStages, sb = i % kBStages;
+        tc_fence_after();
         const uint32_t a0 = tmem + kTmemA + 64 * sa;
         const uint32_t b0 = smem_addr(smem + L.b + sb * b_stage_bytes(NB));
 #pragma unroll
         for (int st = 0; st < 8; ++st)
           umma_ts_f16(tmem, a0 + 8 * st, smem_desc_sw128(b0 + (st >> 2) * (NB * 128) + (st & 3) * 32), idesc,
                       (i > 0 || st > 0) ? 1u : 0u);
+        // the next chunk's operands, polled while these MMAs run
+        const int j = i + 1;
+        if (j < nc) ok = wait_pair(&full_a[j % kAStages], (j / kAStages) & 1, &full_b[j % kBStages], (j / kBStages) & 1);
+        umma_commit(&mma_done[sb]);   // arrives when chunk i's MMAs (and all earlier ones) have completed
       }
-      __syncwarp();
-      if (lane == 0) {   // each arrives when this chunk's MMAs have read their operands
-        umma_commit(&empty_a[sa]);
-        umma_commit(&empty_b[sb]);
-      }
+      umma_commit(done);
+      wait_bounded(done, 0);   // no MMA in flight past this point
     }
     __syncwarp();
-    if (lane == 0) umma_commit(done);
-    __syncwarp();
-    if (ok) wait_bounded(done, 0);   // no MMA in flight past this point
   } else if (warp == kWLoadWarp) {
     // ------------------------------------------------------------------ packed weights
     if (lane == 0) {
@@ -298,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ dequantizing warps
-    const int quarter = warp & 3, par = warp >> 2;   // TMEM lanes 32q.. ; chunks i = par, par + 2, ...
+    const int quarter = warp & 3, hh = warp >> 2;   // TMEM lanes 32q.. ; K half hh of every chunk
     const int row = 32 * quarter + lane;             // row of the tile = TMEM lane
     const int cpg = p.cpg;
     if (!(p.flags & kFlagEarlyWeights) && p.wait_guard) pdl_wait();
@@ -306,46 +315,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g0 = c_begin / cpg, ng = (c_begin + nc - 1) / cpg - g0 + 1;
     uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L.scales);
     {
+      // batches of 16 independent loads in flight (a load-store loop would pay one memory latency per scale)
+      constexpr int kBatch = 16;
       const uint16_t* srow = reinterpret_cast<const uint16_t*>(p.s) + (size_t)min(n0 + row, N - 1) * p.KG + g0;
-      for (int gi = par; gi < ng; gi += 2) sc[row * p.ngroups + gi] = ldg_u16(srow + gi);
+      for (int gb = hh; gb < ng; gb += 2 * kBatch) {
+        uint16_t v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) v[j] = gb + 2 * j < ng ? ldg_u16(srow + gb + 2 * j) : (uint16_t)0;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+          if (gb + 2 * j < ng) sc[row * p.ngroups + gb + 2 * j] = v[j];
+      }
     }
     named_barrier(1, kDequantWarps * 32);
     if (p.wait_guard) pdl_wait();   // the outputs are written in stream order
-    // the row's 64 bytes sit at row * 64 in a weight stage, 16-byte word t at slot t ^ ((row >> 1) & 3)
-    const uint32_t wrow = smem_addr(smem + L.w) + (uint32_t)row * 64;
+    // the row's 64 bytes sit at row * 64 in a weight stage, 16-byte word t at slot t ^ ((row >> 1) & 3); u32 qd
+    // of word t holds the pairs of columns 16qd + t (+4, +8, +12), column j = fp16 weights k 2j, 2j + 1: K half
+    // hh (columns 32hh ..) is u32s 2hh and 2hh + 1 of every word
+    const uint32_t wrow = smem_addr(smem + L.w) + (uint32_t)row * 64 + 8u * hh;
     const uint32_t wsw = (uint32_t)(row >> 1) & 3u;
     const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
-    bool ok = true;
-    for (int i = par; i < nc; i += 2) {
-      const int sw = i % kWStages, sa = i & 1;
-      if (ok) ok = wait_bounded(&full_w[sw], (i / kWStages) & 1);
-      uint4 q[4];
+    // chunk i's words and scale are fetched during chunk i - 1; its fp16 values are computed before waiting for
+    // the tensor-memory stage (chunk i - kAStages's MMAs) to free up
+    uint2 q[4];
+    uint32_t s2 = 0;
+    auto fetch = [&](int i) -> bool {
+      const int sw = i % kWStages;
+      const bool got = wait_bounded(&full_w[sw], (i / kWStages) & 1);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) q[t] = lds128(wrow + sw * kWStageBytes + ((t ^ wsw) << 4));
+      for (int t = 0; t < 4; ++t) q[t] = lds64(wrow + sw * kWStageBytes + ((t ^ wsw) << 4));
+      const int grp = (cpg == 1 ? c_begin + i : (c_begin + i) / cpg) - g0;
+      s2 = (uint32_t)sc[row * p.ngroups + grp] * 0x10001u;
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_w[sw]);
-      const int grp = (cpg == 1 ? c_begin + i : (c_begin + i) / cpg) - g0;
-      const uint32_t s2 = (uint32_t)sc[row * p.ngroups + grp] * 0x10001u;
-      if (i >= 2 && ok) ok = wait_bounded(&empty_a[sa], ((i >> 1) - 1) & 1);
+      return got;
+    };
+    bool ok = nc == 0 || fetch(0);
+    for (int i = 0; i < nc; ++i) {
+      const int sa = i % kAStages;
+      uint32_t v[32];
+#pragma unroll
+      for (int d = 0; d < 2; ++d) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t w = d ? q[t].y : q[t].x;
+          v[16 * d + t] = hmul2_bits(q_pair_lo(w), s2);
+          v[16 * d + 4 + t] = hmul2_bits(q_pair_hi(w), s2);
+          v[16 * d + 8 + t] = hmul2_bits(q_pair_lo(w >> 8), s2);
+          v[16 * d + 12 + t] = hmul2_bits(q_pair_hi(w >> 8), s2);
+        }
+      }
+      if (i + 1 < nc && ok) ok = fetch(i + 1);
+      if (i >= kAStages && ok) {
+        const int c = i - kAStages;   // the chunk whose MMAs last read this stage
+        ok = wait_bounded(&mma_done[c % kBStages], (c / kBStages) & 1);
+      }
       __syncwarp();   // tcgen05.st is warp-collective
       tc_fence_after();
-      // u32 qd of word t holds the pairs of columns 16qd + t (+4, +8, +12): column j = fp16 weights k 2j, 2j + 1
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t v[32];
-#pragma unroll
-        for (int d = 0; d < 2; ++d) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint32_t w = (&q[t].x)[2 * hh + d];
-            v[16 * d + t] = hmul2_bits(q_pair_lo(w), s2);
-            v[16 * d + 4 + t] = hmul2_bits(q_pair_hi(w), s2);
-            v[16 * d + 8 + t] = hmul2_bits(q_pair_lo(w >> 8), s2);
-            v[16 * d + 12 + t] = hmul2_bits(q_pair_hi(w >> 8), s2);
-          }
-        }
-        tmem_st32(tmem + tlane + kTmemA + 64 * sa + 32 * hh, v);
-      }
+      tmem_st32(tmem + tlane + kTmemA + 64 * sa + 32 * hh, v);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&full_a[sa]);
@@ -357,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     float* red = reinterpret_cast<float*>(smem + L.w);   // [m][128] fp32 partials (the weight ring is idle now)
 #pragma unroll
-    for (int blk = par; blk < NB / 16; blk += 2) {
+    for (int blk = hh; blk < NB / 16; blk += 2) {
       const int col0 = blk * 16;
       uint32_t v[16];
       tmem_ld16(tmem + tlane + (uint32_t)col0, v);
