@@ -492,18 +492,126 @@ def profile_case(k, n, m, copies=8, calls=6):
     print(f"profile case K={k} N={n} M={m}: {calls} calls done", file=sys.stderr)
 
 
+# ------------------------------------------------------------------------------------------------ config 3
+
+DECODE_CONTEXT = 512
+
+
+def run_decode(args, rank, world, local):
+    """Config 3: random-init Qwen2.5-3B architecture, all 252 projections INT4 group-128, batch-1 greedy decode with
+    one CUDA graph per step (embedding -> 36 layers -> tied fp16 lm_head -> argmax) after a 512-token prompt of
+    ids uniform over the vocabulary. value = tokens/s on the device; e2e also reads every token back to the host,
+    as a streaming generator does. N > 1: independent replicas (the model fits one GPU; config 4 is the sharded
+    one)."""
+    from lowbit import decode
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    decode.enable_decode_options()
+    steps, warm = min(args.steps, 256), min(args.warmup, 64)
+    m = decode.build(decode.QWEN25_3B, seed=rank)
+    dec = decode.Int4Decoder(m, DECODE_CONTEXT + warm + 2 * steps + 16)
+    int4_bytes = dec.int4_bytes
+    gen = torch.Generator().manual_seed(7 + rank)
+    prompt = torch.randint(0, m.config.vocab_size, (DECODE_CONTEXT,), generator=gen)
+    dec.prefill(prompt)
+    for _ in range(warm):
+        dec.step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        a.record(st)
+        for _ in range(steps):
+            dec.step()
+        b.record(st)
+        b.synchronize()
+        t1 = time.perf_counter()
+    ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    tok_s = steps / (ms / 1e3)
+    # e2e: every step's token read back into pinned host memory before the next step is launched
+    host = torch.empty(1, 1, dtype=torch.long, pin_memory=True)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    for _ in range(steps):
+        dec.step()
+        host.copy_(dec.tok, non_blocking=True)
+        st.synchronize()
+    e2e_s = time.perf_counter() - t2
+    ctx_mid = DECODE_CONTEXT + warm + steps // 2
+    per_tok = int4_bytes + dec.head_bytes() + dec.kv_bytes(ctx_mid)
+    peak, peak_src = measured_peak()
+    achieved = per_tok * tok_s / 1e9
+    line = {
+        "metric": "Qwen2.5-3B decode tokens/s (batch 1, greedy, one CUDA graph per step, 512-token context)",
+        "value": round(tok_s * world, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights x fp16 activations, fp32 accumulate", "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
+        "config": {"workload": "config 3: Qwen2.5-3B architecture, 36 layers, 252 INT4 projections, tied fp16 lm_head",
+                   "model": "Qwen2.5-3B (random init)", "global_batch": world, "seq_len": DECODE_CONTEXT,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "weights 2 GB per token >> 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "algorithmic_bytes_per_token": per_tok,
+                     "bytes": "INT4 projections + fp16 lm_head + KV cache at the mean context"},
+        "e2e": {"value": round(steps / e2e_s * world, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 8, "note": "token read back to pinned host memory after every step"},
+        "clocks": clk.summary(t0, t1),
+        "gpu_launches": dec.launches_per_step() * steps,
+        "cpu_baseline": None,
+    }
+    if dist:
+        dist.barrier()
+        dec.graph = None
+        dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+def profile_decode(steps=3, prompt_len=8):
+    """No timing: the config-3 decoder (Qwen2.5-3B, INT4) with a short prompt, then a few graph steps, for an ncu
+    launch list of whole decode steps."""
+    from lowbit import decode
+    torch.cuda.set_device(0)
+    decode.enable_decode_options()
+    dec = decode.Int4Decoder(decode.build(decode.QWEN25_3B, seed=0), 64)
+    dec.prefill(torch.arange(prompt_len) * 9973 % 151936)
+    for _ in range(steps):
+        dec.step()
+    torch.cuda.synchronize()
+    print(f"profile decode: {dec.launches_per_step()} library launches per step", file=sys.stderr)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=1500)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, choices=(1, 3), default=1,
+                    help="1: M=1 GEMV sweep over the Qwen2.5 projections (headline); 3: Qwen2.5-3B decode tok/s")
     ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",
                     help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
+    if args.profile_decode:
+        profile_decode()
+        return
     if args.profile_case:
         profile_case(*(int(v) for v in args.profile_case.split(",")))
         return
@@ -512,7 +620,12 @@ def main():
     rank, world, local = rank_env()
     if world != args.gpus and world > 1:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
-    line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    elif args.config == 3:
+        line = run_decode(args, rank, world, local)
+    else:
+        line = run_ours(args, rank, world, local)
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -312,4 +312,73 @@ int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, int lay
                   "w4_repack");
 }
 
+// ------------------------------------------------------------------------------------------ decode step
+int lb_decode_embed(const void* emb, const int64_t* tok, void* x, int64_t H, lb_stream_t stream) {
+  if (!emb || !tok || !x) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (H <= 0 || H > (1 << 20)) return fail(LB_ERR_ARGUMENT, "bad hidden size %lld", (long long)H);
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_embed(static_cast<const __half*>(emb), tok, static_cast<__half*>(x), (int)H,
+                                   reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_embed");
+}
+
+int lb_decode_rmsnorm(void* x, const void* r, const void* w, void* h, int64_t H, float eps, lb_stream_t stream) {
+  if (!x || !w || !h) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (H <= 0 || H > (1 << 20)) return fail(LB_ERR_ARGUMENT, "bad hidden size %lld", (long long)H);
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_rmsnorm(static_cast<__half*>(x), static_cast<const __half*>(r),
+                                     static_cast<const __half*>(w), static_cast<__half*>(h), (int)H, eps,
+                                     reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_rmsnorm");
+}
+
+static int check_heads(int nh, int nkv, int hd, int64_t max_len) {
+  if (nh <= 0 || nkv <= 0 || nh % nkv) return fail(LB_ERR_ARGUMENT, "head counts %d / %d", nh, nkv);
+  if (hd <= 0 || hd % 2 || hd > 1024) return fail(LB_ERR_ARGUMENT, "head dim %d must be even and <= 1024", hd);
+  if (max_len <= 0 || max_len > (1 << 24)) return fail(LB_ERR_ARGUMENT, "bad cache length %lld", (long long)max_len);
+  return 0;
+}
+
+int lb_decode_qkv_rope(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos, void* q_out,
+                       void* k_cache, void* v_cache, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream) {
+  if (!qkv || !inv_freq || !pos || !q_out || !k_cache || !v_cache) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  int rc = check_heads(nh, nkv, hd, max_len);
+  if (rc) return rc;
+  if ((rc = check_device())) return rc;
+  return launched(lb::launch_qkv_rope(static_cast<const __half*>(qkv), static_cast<const __half*>(bias), inv_freq, pos,
+                                      static_cast<__half*>(q_out), static_cast<__half*>(k_cache),
+                                      static_cast<__half*>(v_cache), nh, nkv, hd, (int)max_len,
+                                      reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_qkv_rope");
+}
+
+int lb_decode_attention_splits(int64_t max_len) { return max_len > 0 ? lb::attn_splits((int)max_len) : 0; }
+
+int lb_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, float* part_o,
+                        float* part_ml, void* out, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !pos || !part_o || !part_ml || !out)
+    return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  int rc = check_heads(nh, nkv, hd, max_len);
+  if (rc) return rc;
+  if ((nh / nkv) * (hd + 64) * 4 > 48 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
+  if ((rc = check_device())) return rc;
+  return launched(lb::launch_attention(static_cast<const __half*>(q), static_cast<const __half*>(k_cache),
+                                       static_cast<const __half*>(v_cache), pos, part_o, part_ml,
+                                       static_cast<__half*>(out), nh, nkv, hd, (int)max_len,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_attention");
+}
+
+int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {
+  if (!gu || !a) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (I <= 0 || I > (1 << 28)) return fail(LB_ERR_ARGUMENT, "bad size %lld", (long long)I);
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_silu_mul(static_cast<const __half*>(gu), static_cast<__half*>(a), (int)I,
+                                      reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_silu_mul");
+}
+
 }  // extern "C"

@@ -1,0 +1,288 @@
+"""Batch-1 greedy decode of a random-init Qwen2.5-architecture decoder through the INT4 kernels.
+
+The measurement of the reference's bench/e2e.py (`speed_graph`, bench/e2e.py:84-147) -- every decode step (one token
+through all layers, the lm_head and the argmax) captured as one CUDA graph over a static KV cache and replayed --
+without checkpoint or dataset: weights come from the transformers Qwen2 initializer (N(0, 0.02)) and prompt ids are
+uniform over the vocabulary, so the bytes moved per token are those of the real model.
+
+`Int4Decoder` is the product path: the model's projections quantized once (q|k|v and gate|up fused row-wise into
+one INT4 weight each: rows quantize independently, so the bits equal the separate layers'), the decode-step kernels
+of the library around the INT4 GEMVs, and position / token in device memory so a graph replays every step.
+`GraphDecoder` (transformers forward + W4Linear, as the reference runs it) is kept for comparison; with
+transformers 5.5 a captured transformers step replays wrong logits for the fp16 model too, so it is not timed.
+"""
+import torch
+
+from . import model as lbm
+from . import ops
+
+# Qwen2.5 architectures of the benchmark configs (head_dim 128, RMSNorm eps 1e-6, RoPE theta 1e6, SwiGLU)
+QWEN25_3B = dict(hidden_size=2048, intermediate_size=11008, num_hidden_layers=36, num_attention_heads=16,
+                 num_key_value_heads=2, vocab_size=151936, tie_word_embeddings=True)
+QWEN25_7B = dict(hidden_size=3584, intermediate_size=18944, num_hidden_layers=28, num_attention_heads=28,
+                 num_key_value_heads=4, vocab_size=152064, tie_word_embeddings=False)
+
+
+def qwen2_config(arch, **overrides):
+    from transformers import Qwen2Config
+    kw = dict(arch, rms_norm_eps=1e-6, max_position_embeddings=32768,
+              rope_parameters={"rope_type": "default", "rope_theta": 1e6})
+    kw.update(overrides)
+    cfg = Qwen2Config(**kw)
+    cfg._attn_implementation = "sdpa"
+    return cfg
+
+
+@torch.no_grad()
+def build(arch, seed=0, device="cuda", **overrides):
+    """A random-init fp16 Qwen2ForCausalLM, initialized directly on `device`."""
+    from transformers import Qwen2ForCausalLM
+    cfg = qwen2_config(arch, **overrides)
+    torch.manual_seed(seed)
+    with torch.device(device):
+        m = Qwen2ForCausalLM(cfg)
+    return m.half().eval()
+
+
+def to_int4(model, group=128):
+    """Quantize every decoder projection on the GPU and swap in W4Linear; returns (layers, INT4 bytes)."""
+    return lbm.apply_int4(lbm.quantize_layers(model, group), group)
+
+
+def to_fake_quant(model, group=128):
+    """The same quantized values as fp16 nn.Linear weights (cuBLAS on the dequantized weights)."""
+    lbm.apply_fake_quant(lbm.quantize_layers(model, group), group)
+    return model
+
+
+def bytes_per_token(model, context, int4_bytes):
+    """HBM bytes one decode step must read: INT4 projections + fp16 lm_head + the KV cache at `context`."""
+    cfg = model.config
+    head = model.lm_head.weight.numel() * 2
+    kv = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * (cfg.hidden_size // cfg.num_attention_heads) * 2 * context
+    return int4_bytes + head + kv
+
+
+class GraphDecoder:
+    """Static-cache greedy decoding, one CUDA graph per step (bench/e2e.py:84-147). The token fed and its cache
+    position live in static device tensors that the step itself advances, so replays need no host work."""
+
+    def __init__(self, model, max_len):
+        from transformers import StaticCache
+        self.model, self.max_len = model, max_len
+        self.cache = StaticCache(config=model.config, max_cache_len=max_len)
+        dev = model.model.embed_tokens.weight.device
+        self.tok = torch.zeros(1, 1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.logits = None
+        self.graph = None
+
+    def _step(self):
+        out = self.model(input_ids=self.tok, past_key_values=self.cache, cache_position=self.pos, use_cache=True)
+        self.logits = out.logits[:, -1]
+        self.tok.copy_(self.logits.argmax(-1, keepdim=True))
+        self.pos.add_(1)
+
+    @torch.no_grad()
+    def prefill(self, ids):
+        """Run the prompt [1, p] eagerly into the cache; the next token to feed is its greedy continuation."""
+        self.cache.reset()
+        p = ids.shape[1]
+        out = self.model(input_ids=ids, past_key_values=self.cache,
+                         cache_position=torch.arange(p, device=ids.device), use_cache=True)
+        self.tok.copy_(out.logits[:, -1].argmax(-1, keepdim=True))
+        self.pos.fill_(p)
+        return out.logits[0, -1]
+
+    @torch.no_grad()
+    def capture(self):
+        """Warm the step up on a side stream, then capture it. Warm-up writes cache slots that the real steps
+        overwrite, and the token / position are restored."""
+        tok, pos = self.tok.clone(), self.pos.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.tok.copy_(tok)
+        self.pos.copy_(pos)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step()
+        self.graph = g
+        self.tok.copy_(tok)
+        self.pos.copy_(pos)
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.graph.replay()
+
+    @torch.no_grad()
+    def forced(self, seq):
+        """Logits of the graph step for each token of `seq` fed in turn (teacher forcing), float32 [len, vocab]."""
+        rows = []
+        for t in seq:
+            self.tok.fill_(int(t))
+            self.graph.replay()
+            rows.append(self.logits[0].float().clone())
+        return torch.stack(rows)
+
+
+def enable_decode_options():
+    """PDL chaining between the library's kernels, weights fetched before the stream dependency (they are static
+    model state)."""
+    e = ops.ext()
+    e.set_option("pdl", 1)
+    e.set_option("early_weights", 1)
+
+
+class Int4Decoder:
+    """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm, q|k|v GEMV, bias + RoPE + KV
+    append, split attention, o GEMV, residual + RMSNorm, gate|up GEMV, SiLU*up, down GEMV] -> final RMSNorm ->
+    fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
+    projections) and frees its decoder layers."""
+
+    def __init__(self, model, max_len, group=128):
+        e = ops.ext()
+        self.lib = e.lib
+        cfg = model.config
+        self.H, self.I = cfg.hidden_size, cfg.intermediate_size
+        self.nh, self.nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.hd = self.H // self.nh
+        self.eps = float(cfg.rms_norm_eps)
+        self.max_len = max_len
+        theta = float(cfg.rope_parameters["rope_theta"])
+        dev = model.model.embed_tokens.weight.device
+        self.device = dev
+        hd = self.hd
+
+        def w4(weight):
+            packed, scales = ops.quantize_w4_gpu(weight, group)
+            return ops.W4Weight(packed, scales, group, ("mma",))
+
+        self.layers, self.int4_bytes = [], 0
+        with torch.no_grad():
+            for layer in model.model.layers:
+                a, m = layer.self_attn, layer.mlp
+                ly = {
+                    "qkv": w4(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)),
+                    "bias": None if a.q_proj.bias is None else
+                    torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).half().contiguous(),
+                    "o": w4(a.o_proj.weight),
+                    "gu": w4(torch.cat([m.gate_proj.weight, m.up_proj.weight], 0)),
+                    "down": w4(m.down_proj.weight),
+                    "ln1": layer.input_layernorm.weight.detach().half().contiguous(),
+                    "ln2": layer.post_attention_layernorm.weight.detach().half().contiguous(),
+                    "k": torch.zeros(self.nkv, max_len, hd, dtype=torch.half, device=dev),
+                    "v": torch.zeros(self.nkv, max_len, hd, dtype=torch.half, device=dev),
+                }
+                self.int4_bytes += sum(ly[k].nbytes() for k in ("qkv", "o", "gu", "down"))
+                self.layers.append(ly)
+        model.model.layers = None          # the fp16 projections are no longer needed
+        torch.cuda.empty_cache()
+        self.embed = model.model.embed_tokens.weight.detach()
+        self.head = model.lm_head.weight.detach()
+        self.norm = model.model.norm.weight.detach().half().contiguous()
+        self.inv_freq = (1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))).to(dev)
+        self.tok = torch.zeros(1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.x = torch.zeros(self.H, dtype=torch.half, device=dev)
+        self.h = torch.zeros(self.H, dtype=torch.half, device=dev)
+        self.q = torch.zeros(self.nh * hd, dtype=torch.half, device=dev)
+        self.attn = torch.zeros(1, self.nh * hd, dtype=torch.half, device=dev)
+        self.act = torch.zeros(1, self.I, dtype=torch.half, device=dev)
+        splits = self.lib.lb_decode_attention_splits(max_len)
+        self.part_o = torch.zeros(self.nh * splits * hd, dtype=torch.float32, device=dev)
+        self.part_ml = torch.zeros(self.nh * splits * 2, dtype=torch.float32, device=dev)
+        self.logits = None
+        self.graph = None
+
+    def _ok(self, rc):
+        if rc:
+            raise RuntimeError(self.lib.lb_last_error().decode())
+
+    def head_bytes(self):
+        return self.head.numel() * 2
+
+    def kv_bytes(self, context):
+        return 2 * len(self.layers) * self.nkv * self.hd * 2 * context
+
+    def _step(self):
+        L, st = self.lib, torch.cuda.current_stream(self.device).cuda_stream
+        nh, nkv, hd, H = self.nh, self.nkv, self.hd, self.H
+        self._ok(L.lb_decode_embed(self.embed.data_ptr(), self.tok.data_ptr(), self.x.data_ptr(), H, st))
+        h2 = self.h.view(1, H)
+        resid = None
+        for ly in self.layers:
+            self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, ly["ln1"].data_ptr(), self.h.data_ptr(), H,
+                                         self.eps, st))
+            qkv = ops.gemv(h2, ly["qkv"], 6)
+            self._ok(L.lb_decode_qkv_rope(qkv.data_ptr(), None if ly["bias"] is None else ly["bias"].data_ptr(),
+                                          self.inv_freq.data_ptr(), self.pos.data_ptr(), self.q.data_ptr(),
+                                          ly["k"].data_ptr(), ly["v"].data_ptr(), nh, nkv, hd, self.max_len, st))
+            self._ok(L.lb_decode_attention(self.q.data_ptr(), ly["k"].data_ptr(), ly["v"].data_ptr(),
+                                           self.pos.data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
+                                           self.attn.data_ptr(), nh, nkv, hd, self.max_len, st))
+            o = ops.gemv(self.attn, ly["o"], 6)
+            self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), o.data_ptr(), ly["ln2"].data_ptr(), self.h.data_ptr(), H,
+                                         self.eps, st))
+            gu = ops.gemv(h2, ly["gu"], 6)
+            self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
+            d = ops.gemv(self.act, ly["down"], 6)
+            resid = d.data_ptr()
+        self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))
+        self.logits = torch.nn.functional.linear(h2, self.head)
+        self.tok.copy_(self.logits.argmax(-1))
+        self.pos.add_(1)
+
+    def launches_per_step(self):
+        """Kernels of this library per step (the lm_head GEMV and the argmax are cuBLAS / torch)."""
+        return 1 + len(self.layers) * 10 + 1
+
+    @torch.no_grad()
+    def capture(self):
+        """Capture the step (after a warm-up on a side stream; token, position and cache row are restored)."""
+        tok, pos = self.tok.clone(), self.pos.clone()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.tok.copy_(tok)
+        self.pos.copy_(pos)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step()
+        self.graph = g
+        self.tok.copy_(tok)
+        self.pos.copy_(pos)
+        torch.cuda.synchronize(self.device)
+
+    def step(self):
+        self.graph.replay()
+
+    @torch.no_grad()
+    def prefill(self, ids):
+        """Feed the prompt one token per graph step (ids: 1-D or [1, p]); the next token is its greedy
+        continuation. Returns the last prompt token's logits."""
+        ids = ids.reshape(-1).tolist()
+        self.pos.fill_(0)
+        if self.graph is None:
+            self.capture()
+        for t in ids:
+            self.tok.fill_(int(t))
+            self.graph.replay()
+        return self.logits[0]
+
+    @torch.no_grad()
+    def forced(self, seq):
+        """Logits after each token of `seq` fed in turn (teacher forcing), float32 [len, vocab]."""
+        rows = []
+        for t in seq:
+            self.tok.fill_(int(t))
+            self.graph.replay()
+            rows.append(self.logits[0].float().clone())
+        return torch.stack(rows)
