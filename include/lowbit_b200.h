@@ -125,22 +125,22 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  * time, so a captured CUDA graph replays every step. All tensors are fp16 device arrays unless stated.
  *
  * lb_decode_embed:     x[H] = emb[*tok][:]                       (tok: int64 on the device)
- * lb_decode_rmsnorm:   if r: x = x + r; h = w * fp16(x * rsqrt(mean(x^2) + eps))   (Qwen2RMSNorm)
- * lb_decode_qkv_rope:  qkv = [q (nh x hd) | k (nkv x hd) | v (nkv x hd)] + bias (may be NULL); q, k rotated by
- *                      the rotate-half RoPE at angle pos * inv_freq[j] (fp32 [hd/2]); q -> q_out [nh, hd];
- *                      k, v -> caches [nkv, max_len, hd] at row pos
- * lb_decode_attention: one query token over cache rows 0..pos, grouped heads (nh % nkv == 0), scale 1/sqrt(hd);
+ * lb_decode_rmsnorm:   if r: x = x + r; h = w * fp16(x * rsqrt(mean(x^2) + eps))   (Qwen2RMSNorm); H % 8 == 0,
+ *                      all four arrays 16-byte aligned (r may be NULL)
+ * lb_decode_attention: qkv = [q (nh x hd) | k (nkv x hd) | v (nkv x hd)] of the fused projection, + bias (may be
+ *                      NULL); q and k rotated by the rotate-half RoPE at angle pos * inv_freq[j] (fp32 [hd/2]);
+ *                      k, v appended to the caches [nkv, max_len, hd] at row pos; then one query token attends
+ *                      to rows 0..pos (grouped heads, nh % nkv == 0, scale 1/sqrt(hd)) -> out [nh, hd].
  *                      part_o (fp32, nh * lb_decode_attention_splits(max_len) * hd) and part_ml (fp32, twice
- *                      nh * splits) are caller-owned scratch; out [nh, hd]
+ *                      nh * splits) are caller-owned scratch; caches and part_o 16-byte aligned
  * lb_decode_silu_mul:  a[I] = fp16(silu(gu[i])) * gu[I + i]     (gu = [gate | up])
  */
 LB_API int lb_decode_embed(const void* emb, const int64_t* tok, void* x, int64_t H, lb_stream_t stream);
 LB_API int lb_decode_rmsnorm(void* x, const void* r, const void* w, void* h, int64_t H, float eps, lb_stream_t stream);
-LB_API int lb_decode_qkv_rope(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos, void* q_out,
-                       void* k_cache, void* v_cache, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream);
 LB_API int lb_decode_attention_splits(int64_t max_len);
-LB_API int lb_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, float* part_o,
-                        float* part_ml, void* out, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream);
+LB_API int lb_decode_attention(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos,
+                        void* k_cache, void* v_cache, float* part_o, float* part_ml, void* out, int nh, int nkv,
+                        int hd, int64_t max_len, lb_stream_t stream);
 LB_API int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream);
 
 #ifdef __cplusplus

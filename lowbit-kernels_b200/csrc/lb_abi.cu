@@ -325,7 +325,12 @@ int lb_decode_embed(const void* emb, const int64_t* tok, void* x, int64_t H, lb_
 
 int lb_decode_rmsnorm(void* x, const void* r, const void* w, void* h, int64_t H, float eps, lb_stream_t stream) {
   if (!x || !w || !h) return fail(LB_ERR_ARGUMENT, "null pointer argument");
-  if (H <= 0 || H > (1 << 20)) return fail(LB_ERR_ARGUMENT, "bad hidden size %lld", (long long)H);
+  if (H <= 0 || H % 8 || H > lb::rmsnorm_max_hidden())
+    return fail(LB_ERR_ARGUMENT, "hidden size %lld must be a positive multiple of 8 up to %d", (long long)H,
+                lb::rmsnorm_max_hidden());
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(w) |
+        reinterpret_cast<uintptr_t>(h)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "x, r, w and h must be 16-byte aligned");
   int rc = check_device();
   if (rc) return rc;
   return launched(lb::launch_rmsnorm(static_cast<__half*>(x), static_cast<const __half*>(r),
@@ -341,31 +346,23 @@ static int check_heads(int nh, int nkv, int hd, int64_t max_len) {
   return 0;
 }
 
-int lb_decode_qkv_rope(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos, void* q_out,
-                       void* k_cache, void* v_cache, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream) {
-  if (!qkv || !inv_freq || !pos || !q_out || !k_cache || !v_cache) return fail(LB_ERR_ARGUMENT, "null pointer argument");
-  int rc = check_heads(nh, nkv, hd, max_len);
-  if (rc) return rc;
-  if ((rc = check_device())) return rc;
-  return launched(lb::launch_qkv_rope(static_cast<const __half*>(qkv), static_cast<const __half*>(bias), inv_freq, pos,
-                                      static_cast<__half*>(q_out), static_cast<__half*>(k_cache),
-                                      static_cast<__half*>(v_cache), nh, nkv, hd, (int)max_len,
-                                      reinterpret_cast<cudaStream_t>(stream)),
-                  "decode_qkv_rope");
-}
-
 int lb_decode_attention_splits(int64_t max_len) { return max_len > 0 ? lb::attn_splits((int)max_len) : 0; }
 
-int lb_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, float* part_o,
-                        float* part_ml, void* out, int nh, int nkv, int hd, int64_t max_len, lb_stream_t stream) {
-  if (!q || !k_cache || !v_cache || !pos || !part_o || !part_ml || !out)
+int lb_decode_attention(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos, void* k_cache,
+                        void* v_cache, float* part_o, float* part_ml, void* out, int nh, int nkv, int hd,
+                        int64_t max_len, lb_stream_t stream) {
+  if (!qkv || !inv_freq || !pos || !k_cache || !v_cache || !part_o || !part_ml || !out)
     return fail(LB_ERR_ARGUMENT, "null pointer argument");
   int rc = check_heads(nh, nkv, hd, max_len);
   if (rc) return rc;
-  if ((nh / nkv) * (hd + 64) * 4 > 48 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
+  if (hd % 8) return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8", hd);
+  if (lb::attn_smem_bytes(nh, nkv, hd) > 200 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
+  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+        reinterpret_cast<uintptr_t>(part_o)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "caches and part_o must be 16-byte aligned");
   if ((rc = check_device())) return rc;
-  return launched(lb::launch_attention(static_cast<const __half*>(q), static_cast<const __half*>(k_cache),
-                                       static_cast<const __half*>(v_cache), pos, part_o, part_ml,
+  return launched(lb::launch_attention(static_cast<const __half*>(qkv), static_cast<const __half*>(bias), inv_freq, pos,
+                                       static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), part_o, part_ml,
                                        static_cast<__half*>(out), nh, nkv, hd, (int)max_len,
                                        reinterpret_cast<cudaStream_t>(stream)),
                   "decode_attention");

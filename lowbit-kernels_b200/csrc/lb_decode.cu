@@ -24,78 +24,96 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // x = fp16(x + r) when r is given (the residual add), then h = fp16(w * fp16(x * rsqrt(mean(x^2) + eps)))
-// (Qwen2RMSNorm: the normalized value is rounded to fp16 before the weight multiply)
-__global__ void __launch_bounds__(256) rmsnorm_kernel(__half* x, const __half* r, const __half* w, __half* h, int H,
-                                                      float eps) {
+// (Qwen2RMSNorm: the normalized value is rounded to fp16 before the weight multiply). One CTA; every thread
+// loads its (up to kRmsVec) 8-wide pieces at once and keeps them in registers. H % 8 == 0.
+constexpr int kRmsThreads = 256;
+constexpr int kRmsVec = 4;   // H <= 8192
+
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(__half* __restrict__ x, const __half* __restrict__ r,
+                                                              const __half* __restrict__ w, __half* __restrict__ h,
+                                                              int H, float eps) {
   __shared__ float red[32];
   pdl_launch_dependents();
   pdl_wait();
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = __half2float(x[i]);
-    if (r) {
-      const __half s = __hadd(x[i], r[i]);
-      x[i] = s;
-      v = __half2float(s);
+  const int n8 = H / 8;
+  uint4 xv[kRmsVec], rv[kRmsVec], wv[kRmsVec];
+#pragma unroll
+  for (int j = 0; j < kRmsVec; ++j) {
+    const int i = threadIdx.x + j * kRmsThreads;
+    if (i < n8) {
+      xv[j] = reinterpret_cast<const uint4*>(x)[i];
+      wv[j] = reinterpret_cast<const uint4*>(w)[i];
+      if (r) rv[j] = reinterpret_cast<const uint4*>(r)[i];
     }
-    ss += v * v;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kRmsVec; ++j) {
+    const int i = threadIdx.x + j * kRmsThreads;
+    if (i < n8) {
+      __half2* xh = reinterpret_cast<__half2*>(&xv[j]);
+      if (r) {
+        const __half2* rh = reinterpret_cast<const __half2*>(&rv[j]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xh[k] = __hadd2(xh[k], rh[k]);
+        reinterpret_cast<uint4*>(x)[i] = xv[j];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(xh[k]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
   }
   const float inv = rsqrtf(block_sum(ss, red) / (float)H + eps);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const __half n = __float2half_rn(__half2float(x[i]) * inv);
-    h[i] = __float2half_rn(__half2float(w[i]) * __half2float(n));
+#pragma unroll
+  for (int j = 0; j < kRmsVec; ++j) {
+    const int i = threadIdx.x + j * kRmsThreads;
+    if (i < n8) {
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv[j]);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv[j]);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(xh[k]);
+        const __half2 n = __floats2half2_rn(f.x * inv, f.y * inv);
+        oh[k] = __hmul2(wh[k], n);
+      }
+      reinterpret_cast<uint4*>(h)[i] = o;
+    }
   }
 }
 
-// qkv = [q (nh heads) | k (nkv) | v (nkv)] from the fused projection: add the bias, rotate q and k by the
-// position's angles (rotate-half pairing: dims j and j + hd/2), write q and append k, v to the cache at pos.
-// Grid: nh + 2 * nkv heads; block: hd / 2 threads.
-__global__ void qkv_rope_kernel(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos_p,
-                                __half* q_out, __half* kc, __half* vc, int nh, int nkv, int hd, int max_len) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int head = blockIdx.x, j = threadIdx.x, half = hd / 2;
-  const int pos = (int)*pos_p;
-  const __half* src = qkv + (size_t)head * hd;
-  const __half* bsrc = bias ? bias + (size_t)head * hd : nullptr;
-  __half a = src[j], b = src[j + half];
-  if (bsrc) {
-    a = __hadd(a, bsrc[j]);
-    b = __hadd(b, bsrc[j + half]);
-  }
-  if (head >= nh + nkv) {   // v: straight into the cache
-    __half* dst = vc + ((size_t)(head - nh - nkv) * max_len + pos) * hd;
-    dst[j] = a;
-    dst[j + half] = b;
-    return;
-  }
-  float s, c;
-  sincosf((float)pos * inv_freq[j], &s, &c);
-  const float fa = __half2float(a), fb = __half2float(b);
-  const __half ra = __float2half_rn(fa * c - fb * s), rb = __float2half_rn(fb * c + fa * s);
-  __half* dst = head < nh ? q_out + (size_t)head * hd : kc + ((size_t)(head - nh) * max_len + pos) * hd;
-  dst[j] = ra;
-  dst[j + half] = rb;
-}
-
-// Split attention for one query token: CTA (kv head, split) scores positions [64 s, 64 s + 64) of the cache
-// (those <= pos) for the group's query heads, and writes the split's running max, sum of exponentials and
-// unnormalized output (fp32) for attn_combine_kernel.
+// Split attention for one query token, fused with the q|k|v epilogue. CTA (kv head, split) takes cache positions
+// [64 s, 64 s + 64) that are <= pos:
+//   * q of the group's heads = RoPE(qkv + bias) (rotate-half pairing: dims j and j + hd/2, angle pos *
+//     inv_freq[j]), in fp32 shared memory, pre-multiplied by the softmax scale;
+//   * the CTA whose range holds pos also rotates k, and writes k and v (+ bias) into the caches at row pos;
+//   * the range's K and V rows are staged in shared memory with 16-byte loads (row pos from the values just made);
+//   * writes the split's running max, sum of exponentials and unnormalized output (fp32) for attn_combine_kernel.
 constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 256;
 
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* q, const __half* kc, const __half* vc,
-                                                                  const int64_t* pos_p, float* part_o, float* part_ml,
-                                                                  int nh, int nkv, int hd, int max_len, float scale) {
-  extern __shared__ float sm[];   // q [g][hd] fp32, scores [g][chunk]
+__device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& ra, float& rb) {
+  ra = a * c - b * s;
+  rb = b * c + a * s;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* __restrict__ qkv,
+                                                                  const __half* __restrict__ bias,
+                                                                  const float* __restrict__ inv_freq,
+                                                                  const int64_t* __restrict__ pos_p, __half* kc,
+                                                                  __half* vc, float* __restrict__ part_o,
+                                                                  float* __restrict__ part_ml, int nh, int nkv, int hd,
+                                                                  int max_len, float scale) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
   pdl_launch_dependents();
   pdl_wait();
   const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
-  const int g = nh / nkv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32;
-  const int L = (int)*pos_p + 1;
+  const int g = nh / nkv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32, half = hd / 2;
+  const int pos = (int)*pos_p, L = pos + 1;
   const int p0 = split * kAttnChunk, np = min(kAttnChunk, L - p0);
-  float* sq = sm;
-  float* ss = sm + g * hd;
   const size_t pbase = ((size_t)kvh * nsplit + split) * g;
   if (np <= 0) {   // nothing cached here yet: an empty partial
     for (int i = threadIdx.x; i < g; i += blockDim.x) {
@@ -104,22 +122,82 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     }
     return;
   }
-  for (int i = threadIdx.x; i < g * hd; i += blockDim.x) sq[i] = __half2float(q[(size_t)kvh * g * hd + i]) * scale;
-  __syncthreads();
-  const __half* kb = kc + ((size_t)kvh * max_len + p0) * hd;
-  const __half* vb = vc + ((size_t)kvh * max_len + p0) * hd;
-  // scores: warp per position, lanes over the head dimension
-  for (int p = warp; p < np; p += nw) {
-    const __half* kr = kb + (size_t)p * hd;
-    for (int h = 0; h < g; ++h) {
-      float d = 0.f;
-      for (int e = lane; e < hd; e += 32) d += sq[h * hd + e] * __half2float(kr[e]);
-      d = warp_sum(d);
-      if (lane == 0) ss[h * kAttnChunk + p] = d;
+  __half* sk = reinterpret_cast<__half*>(sm_raw);               // [64][hd]
+  __half* sv = sk + kAttnChunk * hd;                             // [64][hd]
+  float* sq = reinterpret_cast<float*>(sv + kAttnChunk * hd);    // [g][hd]
+  float* ss = sq + g * hd;                                       // [g][64]
+  // cached rows (those < pos) of the range
+  const int ncached = min(np, pos - p0), vec = hd / 8;
+  const uint4* kg = reinterpret_cast<const uint4*>(kc + ((size_t)kvh * max_len + p0) * hd);
+  const uint4* vg = reinterpret_cast<const uint4*>(vc + ((size_t)kvh * max_len + p0) * hd);
+  for (int i = threadIdx.x; i < ncached * vec; i += blockDim.x) {
+    reinterpret_cast<uint4*>(sk)[i] = kg[i];
+    reinterpret_cast<uint4*>(sv)[i] = vg[i];
+  }
+  // q of the group's heads, and (in the range holding pos) this token's k and v
+  const bool mine = pos < p0 + kAttnChunk;
+  for (int i = threadIdx.x; i < (g + (mine ? 2 : 0)) * half; i += blockDim.x) {
+    const int hh = i / half, j = i - hh * half;
+    const int head = hh < g ? kvh * g + hh : hh == g ? nh + kvh : nh + nkv + kvh;   // q / k / v row of qkv
+    const __half* src = qkv + (size_t)head * hd;
+    float a = __half2float(src[j]), b = __half2float(src[j + half]);
+    if (bias) {
+      a = __half2float(__hadd(src[j], bias[(size_t)head * hd + j]));
+      b = __half2float(__hadd(src[j + half], bias[(size_t)head * hd + j + half]));
+    }
+    if (hh == g + 1) {   // v: no rotation
+      const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+      sv[(pos - p0) * hd + j] = ha;
+      sv[(pos - p0) * hd + j + half] = hb;
+      vc[((size_t)kvh * max_len + pos) * hd + j] = ha;
+      vc[((size_t)kvh * max_len + pos) * hd + j + half] = hb;
+      continue;
+    }
+    float sn, cs;
+    sincosf((float)pos * inv_freq[j], &sn, &cs);
+    float ra, rb;
+    rope_pair(a, b, cs, sn, ra, rb);
+    const __half ha = __float2half_rn(ra), hb = __float2half_rn(rb);
+    if (hh < g) {   // q rounded to fp16 like the reference path, then scaled in fp32
+      sq[hh * hd + j] = __half2float(ha) * scale;
+      sq[hh * hd + j + half] = __half2float(hb) * scale;
+    } else {
+      sk[(pos - p0) * hd + j] = ha;
+      sk[(pos - p0) * hd + j + half] = hb;
+      kc[((size_t)kvh * max_len + pos) * hd + j] = ha;
+      kc[((size_t)kvh * max_len + pos) * hd + j + half] = hb;
     }
   }
   __syncthreads();
-  // per head: max and exponentials (warp h handles head h, h + nw, ...)
+  // scores: warp per position, lane over 4 consecutive dims of every query head of the group. Every lane runs the
+  // same number of 128-dim rounds (lanes past hd contribute zero), so the full-warp reductions are reached by all
+  // 32 lanes whatever hd is.
+  for (int p = warp; p < np; p += nw) {
+    for (int base = 0; base < hd; base += 128) {
+      const int e0 = base + lane * 4;
+      const bool in = e0 < hd;
+      float2 k01 = make_float2(0.f, 0.f), k23 = make_float2(0.f, 0.f);
+      if (in) {
+        const uint2 kr = *reinterpret_cast<const uint2*>(sk + p * hd + e0);
+        k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+        k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+      }
+      for (int h = 0; h < g; ++h) {
+        float d = 0.f;
+        if (in) {
+          const float4 qv = *reinterpret_cast<const float4*>(sq + h * hd + e0);
+          d = qv.x * k01.x + qv.y * k01.y + qv.z * k23.x + qv.w * k23.y;
+        }
+        d = warp_sum(d);
+        if (lane == 0) {
+          if (base == 0) ss[h * kAttnChunk + p] = d;
+          else ss[h * kAttnChunk + p] += d;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // per head: max and exponentials (warp h handles heads h, h + nw, ...)
   for (int h = warp; h < g; h += nw) {
     float m = -INFINITY;
     for (int p = lane; p < np; p += 32) m = fmaxf(m, ss[h * kAttnChunk + p]);
@@ -138,12 +216,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     }
   }
   __syncthreads();
-  // unnormalized outputs: thread (h, e) sums over the split's positions
-  for (int i = threadIdx.x; i < g * hd; i += blockDim.x) {
-    const int h = i / hd, e = i - h * hd;
-    float acc = 0.f;
-    for (int p = 0; p < np; ++p) acc += ss[h * kAttnChunk + p] * __half2float(vb[(size_t)p * hd + e]);
-    part_o[(pbase + h) * hd + e] = acc;
+  // unnormalized outputs: thread (h, 4 dims) sums over the range's positions
+  const int q4 = hd / 4;
+  for (int i = threadIdx.x; i < g * q4; i += blockDim.x) {
+    const int h = i / q4, e0 = (i - h * q4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < np; ++p) {
+      const float w = ss[h * kAttnChunk + p];
+      const uint2 vr = *reinterpret_cast<const uint2*>(sv + p * hd + e0);
+      const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+      const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
+      acc.x += w * v01.x;
+      acc.y += w * v01.y;
+      acc.z += w * v23.x;
+      acc.w += w * v23.y;
+    }
+    *reinterpret_cast<float4*>(part_o + (pbase + h) * hd + e0) = acc;
   }
 }
 
@@ -204,23 +292,27 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
 }  // namespace
 
 cudaError_t launch_rmsnorm(__half* x, const __half* r, const __half* w, __half* h, int H, float eps, cudaStream_t st) {
-  return launch_pdl(rmsnorm_kernel, dim3(1), dim3(256), 0, st, x, r, w, h, H, eps);
+  return launch_pdl(rmsnorm_kernel, dim3(1), dim3(kRmsThreads), 0, st, x, r, w, h, H, eps);
 }
 
-cudaError_t launch_qkv_rope(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,
-                            __half* q, __half* kc, __half* vc, int nh, int nkv, int hd, int max_len, cudaStream_t st) {
-  return launch_pdl(qkv_rope_kernel, dim3(nh + 2 * nkv), dim3(hd / 2), 0, st, qkv, bias, inv_freq, pos, q, kc, vc, nh,
-                    nkv, hd, max_len);
-}
+int rmsnorm_max_hidden() { return 8 * kRmsThreads * kRmsVec; }
 
 int attn_splits(int max_len) { return (max_len + kAttnChunk - 1) / kAttnChunk; }
 
-cudaError_t launch_attention(const __half* q, const __half* kc, const __half* vc, const int64_t* pos, float* part_o,
-                             float* part_ml, __half* out, int nh, int nkv, int hd, int max_len, cudaStream_t st) {
-  const int nsplit = attn_splits(max_len), g = nh / nkv;
-  const size_t smem = (size_t)(g * hd + g * kAttnChunk) * sizeof(float);
-  cudaError_t e = launch_pdl(attn_split_kernel, dim3(nkv, nsplit), dim3(kAttnThreads), smem, st, q, kc, vc, pos, part_o,
-                             part_ml, nh, nkv, hd, max_len, 1.f / sqrtf((float)hd));
+size_t attn_smem_bytes(int nh, int nkv, int hd) {
+  const int g = nh / nkv;
+  return (size_t)2 * kAttnChunk * hd * sizeof(__half) + (size_t)(g * hd + g * kAttnChunk) * sizeof(float);
+}
+
+cudaError_t launch_attention(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,
+                             __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,
+                             int hd, int max_len, cudaStream_t st) {
+  const int nsplit = attn_splits(max_len);
+  const size_t smem = attn_smem_bytes(nh, nkv, hd);
+  cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(attn_split_kernel, dim3(nkv, nsplit), dim3(kAttnThreads), smem, st, qkv, bias, inv_freq, pos, kc, vc,
+                 part_o, part_ml, nh, nkv, hd, max_len, 1.f / sqrtf((float)hd));
   if (e != cudaSuccess) return e;
   return launch_pdl(attn_combine_kernel, dim3(nh), dim3(hd), 0, st, (const float*)part_o, (const float*)part_ml, out, nh,
                     nkv, hd, nsplit);

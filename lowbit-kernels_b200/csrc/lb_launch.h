@@ -61,11 +61,12 @@ cudaError_t launch_repack(const uint8_t* canonical, uint8_t* out, int N, int K, 
 // decode-step kernels (lb_decode.cu)
 cudaError_t launch_embed(const __half* emb, const int64_t* tok, __half* x, int H, cudaStream_t st);
 cudaError_t launch_rmsnorm(__half* x, const __half* r, const __half* w, __half* h, int H, float eps, cudaStream_t st);
-cudaError_t launch_qkv_rope(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,
-                            __half* q, __half* kc, __half* vc, int nh, int nkv, int hd, int max_len, cudaStream_t st);
+int rmsnorm_max_hidden();
 int attn_splits(int max_len);
-cudaError_t launch_attention(const __half* q, const __half* kc, const __half* vc, const int64_t* pos, float* part_o,
-                             float* part_ml, __half* out, int nh, int nkv, int hd, int max_len, cudaStream_t st);
+size_t attn_smem_bytes(int nh, int nkv, int hd);
+cudaError_t launch_attention(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,
+                             __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,
+                             int hd, int max_len, cudaStream_t st);
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st);
 
 // tcgen05 skinny GEMM (lb_gemm_tc.cu), M <= 64: per 128-row tile a cluster of `splits` CTAs splitting K.

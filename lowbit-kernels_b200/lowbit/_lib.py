@@ -35,9 +35,8 @@ SIGNATURES = {
     "lb_w4_repack": ([_P, _P, _I64, _I64, _I, _P], _I),
     "lb_decode_embed": ([_P, _P, _P, _I64, _P], _I),
     "lb_decode_rmsnorm": ([_P, _P, _P, _P, _I64, ctypes.c_float, _P], _I),
-    "lb_decode_qkv_rope": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _P], _I),
     "lb_decode_attention_splits": ([_I64], _I),
-    "lb_decode_attention": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _P], _I),
+    "lb_decode_attention": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _P], _I),
     "lb_decode_silu_mul": ([_P, _P, _I64, _P], _I),
 }
 

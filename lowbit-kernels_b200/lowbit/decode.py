@@ -139,8 +139,9 @@ def enable_decode_options():
 
 
 class Int4Decoder:
-    """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm, q|k|v GEMV, bias + RoPE + KV
-    append, split attention, o GEMV, residual + RMSNorm, gate|up GEMV, SiLU*up, down GEMV] -> final RMSNorm ->
+    """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm, q|k|v GEMV, attention (bias +
+    RoPE + KV append + split attention, combine), o GEMV, residual + RMSNorm, gate|up GEMV, SiLU*up, down GEMV] ->
+    final RMSNorm ->
     fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
     projections) and frees its decoder layers."""
 
@@ -190,7 +191,6 @@ class Int4Decoder:
         self.pos = torch.zeros(1, dtype=torch.long, device=dev)
         self.x = torch.zeros(self.H, dtype=torch.half, device=dev)
         self.h = torch.zeros(self.H, dtype=torch.half, device=dev)
-        self.q = torch.zeros(self.nh * hd, dtype=torch.half, device=dev)
         self.attn = torch.zeros(1, self.nh * hd, dtype=torch.half, device=dev)
         self.act = torch.zeros(1, self.I, dtype=torch.half, device=dev)
         splits = self.lib.lb_decode_attention_splits(max_len)
@@ -219,11 +219,9 @@ class Int4Decoder:
             self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, ly["ln1"].data_ptr(), self.h.data_ptr(), H,
                                          self.eps, st))
             qkv = ops.gemv(h2, ly["qkv"], 6)
-            self._ok(L.lb_decode_qkv_rope(qkv.data_ptr(), None if ly["bias"] is None else ly["bias"].data_ptr(),
-                                          self.inv_freq.data_ptr(), self.pos.data_ptr(), self.q.data_ptr(),
-                                          ly["k"].data_ptr(), ly["v"].data_ptr(), nh, nkv, hd, self.max_len, st))
-            self._ok(L.lb_decode_attention(self.q.data_ptr(), ly["k"].data_ptr(), ly["v"].data_ptr(),
-                                           self.pos.data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
+            self._ok(L.lb_decode_attention(qkv.data_ptr(), None if ly["bias"] is None else ly["bias"].data_ptr(),
+                                           self.inv_freq.data_ptr(), self.pos.data_ptr(), ly["k"].data_ptr(),
+                                           ly["v"].data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
                                            self.attn.data_ptr(), nh, nkv, hd, self.max_len, st))
             o = ops.gemv(self.attn, ly["o"], 6)
             self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), o.data_ptr(), ly["ln2"].data_ptr(), self.h.data_ptr(), H,
@@ -239,7 +237,7 @@ class Int4Decoder:
 
     def launches_per_step(self):
         """Kernels of this library per step (the lm_head GEMV and the argmax are cuBLAS / torch)."""
-        return 1 + len(self.layers) * 10 + 1
+        return 1 + len(self.layers) * 9 + 1
 
     @torch.no_grad()
     def capture(self):

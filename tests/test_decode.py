@@ -61,3 +61,86 @@ def test_greedy_continuation_is_the_argmax():
         dec.step()
         assert dec.tok.item() == dec.logits[0].argmax().item()
     assert dec.pos.item() == 24
+
+
+def _lib():
+    return ops.ext().lib
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+@pytest.mark.parametrize("H", [2048, 3584])
+def test_rmsnorm_kernel(H):
+    g = torch.Generator(device="cuda").manual_seed(H)
+    x = torch.randn(H, device="cuda", generator=g).half()
+    r = torch.randn(H, device="cuda", generator=g).half()
+    w = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).half()
+    want_x = x + r
+    n = (want_x.float() * torch.rsqrt(want_x.float().pow(2).mean() + 1e-6)).half()
+    want_h = w * n
+    h = torch.empty_like(x)
+    assert _lib().lb_decode_rmsnorm(x.data_ptr(), r.data_ptr(), w.data_ptr(), h.data_ptr(), H, 1e-6, _stream()) == 0
+    assert torch.equal(x, want_x)      # the residual add is one fp16 rounding, as in torch
+    # the fp32 sum of squares is summed in another order: allow one fp16 ulp
+    ulp = torch.finfo(torch.half).eps * want_h.float().abs().clamp_min(2 ** -14)
+    assert torch.all((h.float() - want_h.float()).abs() <= 2 * ulp)
+
+
+def _rope(t, pos, inv_freq):
+    """rotate-half RoPE (transformers apply_rotary_pos_emb), fp32."""
+    ang = pos * inv_freq
+    c, s = torch.cos(ang), torch.sin(ang)
+    half = t.shape[-1] // 2
+    a, b = t[..., :half], t[..., half:]
+    return torch.cat([a * c - b * s, b * c + a * s], -1)
+
+
+@pytest.mark.parametrize("pos", [0, 63, 64, 257])
+@pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64)])
+def test_fused_attention_kernel(pos, heads):
+    nh, nkv, hd = heads
+    max_len = 320
+    g = torch.Generator(device="cuda").manual_seed(pos + nh)
+    qkv = torch.randn((nh + 2 * nkv) * hd, device="cuda", generator=g).half()
+    bias = (0.1 * torch.randn((nh + 2 * nkv) * hd, device="cuda", generator=g)).half()
+    kc = torch.randn(nkv, max_len, hd, device="cuda", generator=g).half()
+    vc = torch.randn(nkv, max_len, hd, device="cuda", generator=g).half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    inv_freq = (1.0 / (1e6 ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))).cuda()
+    splits = _lib().lb_decode_attention_splits(max_len)
+    part_o = torch.empty(nh * splits * hd, device="cuda")
+    part_ml = torch.empty(nh * splits * 2, device="cuda")
+    out = torch.empty(nh * hd, device="cuda").half()
+    p = torch.tensor([pos], device="cuda")
+    assert _lib().lb_decode_attention(qkv.data_ptr(), bias.data_ptr(), inv_freq.data_ptr(), p.data_ptr(),
+                                      kc.data_ptr(), vc.data_ptr(), part_o.data_ptr(), part_ml.data_ptr(),
+                                      out.data_ptr(), nh, nkv, hd, max_len, _stream()) == 0
+    torch.cuda.synchronize()
+    b = (qkv + bias).float().view(nh + 2 * nkv, hd)
+    q = _rope(b[:nh], pos, inv_freq).half().float()
+    k_new = _rope(b[nh:nh + nkv], pos, inv_freq).half()
+    v_new = b[nh + nkv:].half()
+    # the new row is appended, every other row untouched
+    assert torch.allclose(kc[:, pos].float(), k_new.float(), atol=2e-3, rtol=2e-3)
+    assert torch.equal(vc[:, pos], v_new)
+    keep = torch.ones(max_len, dtype=torch.bool)
+    keep[pos] = False
+    assert torch.equal(kc[:, keep], kc0[:, keep]) and torch.equal(vc[:, keep], vc0[:, keep])
+    K, V = kc[:, :pos + 1].float(), vc[:, :pos + 1].float()
+    grp = nh // nkv
+    Kx, Vx = K.repeat_interleave(grp, 0), V.repeat_interleave(grp, 0)
+    att = torch.softmax((q[:, None, :] @ Kx.transpose(1, 2))[:, 0] / hd ** 0.5, -1)
+    want = (att[:, None, :] @ Vx)[:, 0]
+    assert torch.allclose(out.float().view(nh, hd), want, atol=3e-3, rtol=3e-3)
+
+
+def test_silu_mul_kernel():
+    I = 11008
+    g = torch.Generator(device="cuda").manual_seed(0)
+    gu = (3 * torch.randn(2 * I, device="cuda", generator=g)).half()
+    a = torch.empty(I, device="cuda").half()
+    assert _lib().lb_decode_silu_mul(gu.data_ptr(), a.data_ptr(), I, _stream()) == 0
+    want = torch.nn.functional.silu(gu[:I]) * gu[I:]
+    assert torch.allclose(a.float(), want.float(), atol=1e-3, rtol=2e-3)
