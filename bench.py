@@ -580,6 +580,86 @@ def run_decode(args, rank, world, local):
     return line if rank == 0 else None
 
 
+# ------------------------------------------------------------------------------------------------ config 4
+
+TP_CONTEXT = 1024
+
+
+def run_tp_decode(args, rank, world, local):
+    """Config 4: random-init Qwen2.5-7B architecture, INT4 group-128, tensor-parallel over the torchrun ranks
+    (column-parallel q|k|v and gate|up, row-parallel o and down + NCCL allreduce, vocabulary-parallel lm_head),
+    batch-1 greedy decode with one CUDA graph per step after a 1024-token prompt. value = tokens/s of the whole
+    job (strong scaling: the same model split over more GPUs), timed on the device, max over ranks."""
+    from lowbit import decode
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    decode.enable_decode_options()
+    steps, warm = min(args.steps, 256), min(args.warmup, 64)
+    m = decode.build(decode.QWEN25_7B, seed=0, device=device)
+    dec = decode.Int4Decoder(m, TP_CONTEXT + warm + steps + 16, world=world, rank=rank,
+                             pg=dist.group.WORLD if dist else None)
+    del m
+    torch.cuda.empty_cache()
+    gen = torch.Generator().manual_seed(7)
+    prompt = torch.randint(0, decode.QWEN25_7B["vocab_size"], (TP_CONTEXT,), generator=gen)
+    dec.prefill(prompt)
+    for _ in range(warm):
+        dec.step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        a.record(st)
+        for _ in range(steps):
+            dec.step()
+        b.record(st)
+        b.synchronize()
+        t1 = time.perf_counter()
+    ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    tok_s = steps / (ms / 1e3)
+    ctx_mid = TP_CONTEXT + warm + steps // 2
+    per_rank = dec.int4_bytes + dec.head_bytes() + dec.kv_bytes(ctx_mid)
+    peak, peak_src = measured_peak()
+    achieved = per_rank * tok_s / 1e9       # one rank's HBM traffic rate; every rank reads its own shard
+    line = {
+        "metric": "Qwen2.5-7B tensor-parallel decode tokens/s (batch 1, greedy, one CUDA graph per step, 1024-token context)",
+        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights x fp16 activations, fp32 accumulate",
+        "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
+        "config": {"workload": "config 4: Qwen2.5-7B architecture, 28 layers, INT4 group-128, untied fp16 lm_head",
+                   "model": "Qwen2.5-7B (random init)", "global_batch": 1, "seq_len": TP_CONTEXT,
+                   "parallelism": f"tp{world}: column q|k|v, gate|up; row o, down + NCCL allreduce; vocab lm_head"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "algorithmic_bytes_per_token_per_rank": per_rank,
+                     "bytes": "this rank's INT4 shard + fp16 lm_head rows + KV cache at the mean context"},
+        "e2e": None,
+        "clocks": clk.summary(t0, t1),
+        "gpu_launches": dec.launches_per_step() * steps,
+        "cpu_baseline": None,
+    }
+    if dist:
+        dist.barrier()
+        dec.graph = None
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
 def profile_decode(steps=3, prompt_len=8):
     """No timing: the config-3 decoder (Qwen2.5-3B, INT4) with a short prompt, then a few graph steps, for an ncu
     launch list of whole decode steps."""
@@ -600,8 +680,9 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=1500)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", type=int, choices=(1, 3), default=1,
-                    help="1: M=1 GEMV sweep over the Qwen2.5 projections (headline); 3: Qwen2.5-3B decode tok/s")
+    ap.add_argument("--config", type=int, choices=(1, 3, 4), default=1,
+                    help="1: M=1 GEMV sweep over the Qwen2.5 projections (headline); 3: Qwen2.5-3B decode tok/s; "
+                         "4: Qwen2.5-7B tensor-parallel decode tok/s over the torchrun ranks")
     ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -624,6 +705,8 @@ def main():
         line = run_reference(args, rank, world)
     elif args.config == 3:
         line = run_decode(args, rank, world, local)
+    elif args.config == 4:
+        line = run_tp_decode(args, rank, world, local)
     else:
         line = run_ours(args, rank, world, local)
     if line is not None:

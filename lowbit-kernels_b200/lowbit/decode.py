@@ -145,19 +145,26 @@ class Int4Decoder:
     fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
     projections) and frees its decoder layers."""
 
-    def __init__(self, model, max_len, group=128):
+    def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None):
+        from . import tp
         e = ops.ext()
         self.lib = e.lib
         cfg = model.config
-        self.H, self.I = cfg.hidden_size, cfg.intermediate_size
-        self.nh, self.nkv = cfg.num_attention_heads, cfg.num_key_value_heads
-        self.hd = self.H // self.nh
+        self.H, I = cfg.hidden_size, cfg.intermediate_size
+        nh, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.hd = self.H // nh
         self.eps = float(cfg.rms_norm_eps)
         self.max_len = max_len
+        self.world, self.rank, self.pg = world, rank, pg
         theta = float(cfg.rope_parameters["rope_theta"])
         dev = model.model.embed_tokens.weight.device
         self.device = dev
         hd = self.hd
+        shard = tp.plan(nh, nkv, hd, I, cfg.vocab_size, world, rank)
+        self.nh = shard["q_heads"][1] - shard["q_heads"][0]
+        self.nkv = shard["kv_heads"][1] - shard["kv_heads"][0]
+        self.I = shard["inter"][1] - shard["inter"][0]
+        self.vocab0 = shard["vocab"][0]
 
         def w4(weight):
             packed, scales = ops.quantize_w4_gpu(weight, group)
@@ -167,13 +174,16 @@ class Int4Decoder:
         with torch.no_grad():
             for layer in model.model.layers:
                 a, m = layer.self_attn, layer.mlp
+                w = {"q": a.q_proj.weight, "k": a.k_proj.weight, "v": a.v_proj.weight, "o": a.o_proj.weight,
+                     "gate": m.gate_proj.weight, "up": m.up_proj.weight, "down": m.down_proj.weight,
+                     "q_b": a.q_proj.bias, "k_b": a.k_proj.bias, "v_b": a.v_proj.bias}
+                sh = tp.shard_layer(w, shard)
                 ly = {
-                    "qkv": w4(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)),
-                    "bias": None if a.q_proj.bias is None else
-                    torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).half().contiguous(),
-                    "o": w4(a.o_proj.weight),
-                    "gu": w4(torch.cat([m.gate_proj.weight, m.up_proj.weight], 0)),
-                    "down": w4(m.down_proj.weight),
+                    "qkv": w4(sh["qkv"]),
+                    "bias": None if sh["bias"] is None else sh["bias"].half().contiguous(),
+                    "o": w4(sh["o"]),
+                    "gu": w4(sh["gu"]),
+                    "down": w4(sh["down"]),
                     "ln1": layer.input_layernorm.weight.detach().half().contiguous(),
                     "ln2": layer.post_attention_layernorm.weight.detach().half().contiguous(),
                     "k": torch.zeros(self.nkv, max_len, hd, dtype=torch.half, device=dev),
@@ -184,7 +194,8 @@ class Int4Decoder:
         model.model.layers = None          # the fp16 projections are no longer needed
         torch.cuda.empty_cache()
         self.embed = model.model.embed_tokens.weight.detach()
-        self.head = model.lm_head.weight.detach()
+        v0, v1 = shard["vocab"]
+        self.head = model.lm_head.weight.detach()[v0:v1].contiguous() if world > 1 else model.lm_head.weight.detach()
         self.norm = model.model.norm.weight.detach().half().contiguous()
         self.inv_freq = (1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))).to(dev)
         self.tok = torch.zeros(1, dtype=torch.long, device=dev)
@@ -193,6 +204,8 @@ class Int4Decoder:
         self.h = torch.zeros(self.H, dtype=torch.half, device=dev)
         self.attn = torch.zeros(1, self.nh * hd, dtype=torch.half, device=dev)
         self.act = torch.zeros(1, self.I, dtype=torch.half, device=dev)
+        self.pair = torch.zeros(2, dtype=torch.float32, device=dev)
+        self.pairs = torch.zeros(2 * world, dtype=torch.float32, device=dev)
         splits = self.lib.lb_decode_attention_splits(max_len)
         self.part_o = torch.zeros(self.nh * splits * hd, dtype=torch.float32, device=dev)
         self.part_ml = torch.zeros(self.nh * splits * 2, dtype=torch.float32, device=dev)
@@ -204,9 +217,11 @@ class Int4Decoder:
             raise RuntimeError(self.lib.lb_last_error().decode())
 
     def head_bytes(self):
+        """fp16 lm_head bytes this rank reads per step (its vocabulary rows)."""
         return self.head.numel() * 2
 
     def kv_bytes(self, context):
+        """KV-cache bytes this rank reads per step at `context` cached tokens."""
         return 2 * len(self.layers) * self.nkv * self.hd * 2 * context
 
     def _step(self):
@@ -224,15 +239,28 @@ class Int4Decoder:
                                            ly["v"].data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
                                            self.attn.data_ptr(), nh, nkv, hd, self.max_len, st))
             o = ops.gemv(self.attn, ly["o"], 6)
+            if self.world > 1:
+                torch.distributed.all_reduce(o, group=self.pg)
             self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), o.data_ptr(), ly["ln2"].data_ptr(), self.h.data_ptr(), H,
                                          self.eps, st))
             gu = ops.gemv(h2, ly["gu"], 6)
             self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
             d = ops.gemv(self.act, ly["down"], 6)
+            if self.world > 1:
+                torch.distributed.all_reduce(d, group=self.pg)
             resid = d.data_ptr()
         self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))
         self.logits = torch.nn.functional.linear(h2, self.head)
-        self.tok.copy_(self.logits.argmax(-1))
+        if self.world == 1:
+            self.tok.copy_(self.logits.argmax(-1))
+        else:
+            # vocabulary-parallel argmax: each rank's best (value, global index); the first rank holding the
+            # overall maximum wins, which is the first occurrence over the whole vocabulary
+            val, idx = self.logits.float().max(-1)
+            self.pair.copy_(torch.cat([val, (idx + self.vocab0).float()]))
+            torch.distributed.all_gather_into_tensor(self.pairs, self.pair, group=self.pg)
+            pr = self.pairs.view(self.world, 2)
+            self.tok.copy_(pr[pr[:, 0].argmax(), 1].long().view(1))
         self.pos.add_(1)
 
     def launches_per_step(self):

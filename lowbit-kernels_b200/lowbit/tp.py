@@ -1,0 +1,66 @@
+"""Tensor-parallel sharding of a Qwen2 decoder for INT4 decode (the benchmark's multi-GPU config).
+
+Column-parallel q|k|v (by attention heads) and gate|up (by 128-row groups of the intermediate size), row-parallel
+o and down on the matching 128-column groups -- so every shard's INT4 groups are exactly the unsharded model's and
+the quantized bits are identical -- each followed by one sum allreduce, and a vocabulary-parallel lm_head (local
+argmax, then an all-gather of (value, index) pairs). The reference has no multi-GPU code; this follows its
+layer math (lowbit/model.py:15-27 applied to each shard).
+
+Attention heads: with world <= kv heads each rank takes whole kv heads and their query groups; with more ranks
+than kv heads (Qwen2.5-7B at 8 GPUs: 4 kv heads, 28 query heads), the ranks sharing a kv head each hold a copy of
+it and split its query group (7 heads -> 4 + 3), so every rank keeps one uniform query group per local kv head.
+"""
+GROUP = 128
+
+
+def even_split(n, parts):
+    """[(start, stop)] of `parts` contiguous ranges covering range(n), sizes differing by at most one."""
+    return [(n * i // parts, n * (i + 1) // parts) for i in range(parts)]
+
+
+def plan(nh, nkv, hd, inter, vocab, world, rank):
+    """The shard of `rank`: global q heads, kv heads, intermediate rows (128-aligned) and vocabulary rows."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    if nh % nkv:
+        raise ValueError(f"{nh} query heads do not group over {nkv} kv heads")
+    g = nh // nkv
+    if world <= nkv:
+        if nkv % world:
+            raise ValueError(f"{nkv} kv heads do not divide over {world} ranks")
+        per = nkv // world
+        kv = (rank * per, (rank + 1) * per)
+        q = (kv[0] * g, kv[1] * g)
+    else:
+        if world % nkv:
+            raise ValueError(f"{world} ranks do not divide over {nkv} kv heads")
+        share = world // nkv
+        if share > g:
+            raise ValueError(f"{share} ranks per kv head but only {g} query heads each")
+        head = rank // share
+        lo, hi = even_split(g, share)[rank % share]
+        kv = (head, head + 1)
+        q = (head * g + lo, head * g + hi)
+    if inter % GROUP:
+        raise ValueError(f"intermediate size {inter} is not a multiple of {GROUP}")
+    gl, gh = even_split(inter // GROUP, world)[rank]
+    return {"q_heads": q, "kv_heads": kv, "inter": (gl * GROUP, gh * GROUP),
+            "vocab": even_split(vocab, world)[rank], "hd": hd}
+
+
+def shard_layer(w, p):
+    """Slice one decoder layer's fp16 weights (dict of torch tensors: q, k, v, o, gate, up, down weights and
+    q_b, k_b, v_b biases, nn.Linear [out, in] layout) to the shard `p`. Returns the fused q|k|v rows (+ bias),
+    the o columns, the fused gate|up rows and the down columns."""
+    import torch
+    hd = p["hd"]
+    q0, q1 = p["q_heads"]
+    k0, k1 = p["kv_heads"]
+    i0, i1 = p["inter"]
+    qr, kr = slice(q0 * hd, q1 * hd), slice(k0 * hd, k1 * hd)
+    qkv = torch.cat([w["q"][qr], w["k"][kr], w["v"][kr]], 0)
+    bias = None if w.get("q_b") is None else torch.cat([w["q_b"][qr], w["k_b"][kr], w["v_b"][kr]], 0)
+    return {"qkv": qkv.contiguous(), "bias": bias,
+            "o": w["o"][:, qr].contiguous(),
+            "gu": torch.cat([w["gate"][i0:i1], w["up"][i0:i1]], 0).contiguous(),
+            "down": w["down"][:, i0:i1].contiguous()}
