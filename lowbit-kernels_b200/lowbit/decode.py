@@ -260,7 +260,7 @@ class Int4Decoder:
             self.pair.copy_(torch.cat([val, (idx + self.vocab0).float()]))
             torch.distributed.all_gather_into_tensor(self.pairs, self.pair, group=self.pg)
             pr = self.pairs.view(self.world, 2)
-            self.tok.copy_(pr[pr[:, 0].argmax(), 1].long().view(1))
+            self.tok.copy_(pr[:, 1].gather(0, pr[:, 0].argmax().view(1)).long())   # no host sync
         self.pos.add_(1)
 
     def launches_per_step(self):
