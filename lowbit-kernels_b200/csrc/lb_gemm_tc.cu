@@ -27,8 +27,8 @@
 
 #include <atomic>
 
-#include "lb_common.cuh"
 #include "lb_launch.h"
+#include "lb_tma.cuh"
 
 namespace lb {
 
@@ -83,14 +83,11 @@ struct TcParams {
   int ngroups;     // scale groups staged per CTA (the largest K range's)
 };
 
+// both phases, polled together (each poll of a completed barrier still costs a full shared-memory round trip)
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  atomicExch(&g_tc_status, kErrBarrierTimeout);
-  return false;
+  return lb::wait_bounded(bar, parity, &g_tc_status);
 }
 
-// both phases, polled together (each poll of a completed barrier still costs a full shared-memory round trip)
 __device__ __forceinline__ bool wait_pair(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb) {
   bool da = false, db = false;
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
@@ -152,62 +149,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
       "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
-}
-
-// 2-D tensor copy global -> this CTA's shared memory (coordinates: innermost first), completing on `bar`
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-      "[%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-
-// One loader thread: streams chunks 0..nc-1 of a stage ring, refilling a stage once its consumers released it,
-// then waits for its own last copies so that none is in flight when the CTA exits. Returns false if a wait gave up.
-template <typename Issue>
-__device__ __forceinline__ void run_loader(int nc, int stages, uint64_t* full, uint64_t* empty, uint32_t bytes,
-                                           Issue issue) {
-  int issued = 0;
-  for (int i = 0; i < nc; ++i) {
-    const int s = i % stages;
-    if (i >= stages && !wait_bounded(&empty[s], ((i / stages) - 1) & 1)) break;
-    mbar_arrive_expect_tx(&full[s], bytes);
-    issue(i, s);
-    issued = i + 1;
-  }
-  for (int i = issued > stages ? issued - stages : 0; i < issued; ++i) wait_bounded(&full[i % stages], (i / stages) & 1);
 }
 
 }  // namespace
@@ -285,10 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWLoadWarp) {
     // ------------------------------------------------------------------ packed weights
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+      tma_prefetch_map(&wmap);
       // static weights may be fetched before the stream dependency resolves (kFlagEarlyWeights)
       if (!(p.flags & kFlagEarlyWeights) && p.wait_guard) pdl_wait();
-      run_loader(nc, kWStages, full_w, empty_w, kWStageBytes, [&](int i, int s) {
+      run_loader(nc, kWStages, full_w, empty_w, kWStageBytes, &g_tc_status, [&](int i, int s) {
         tma_load_2d(smem + L.w + s * kWStageBytes, &wmap, (c_begin + i) * 64, n0, &full_w[s]);
       });
     }
@@ -296,9 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kXLoadWarp) {
     // ------------------------------------------------------------------ activations
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+      tma_prefetch_map(&xmap);
       if (p.wait_guard) pdl_wait();   // the activations come from the previous kernel in the stream
-      run_loader(nc, kBStages, full_b, empty_b, b_stage_bytes(NB), [&](int i, int s) {
+      run_loader(nc, kBStages, full_b, empty_b, b_stage_bytes(NB), &g_tc_status, [&](int i, int s) {
         uint8_t* dst = smem + L.b + s * b_stage_bytes(NB);
         tma_load_2d(dst, &xmap, (c_begin + i) * 128, 0, &full_b[s]);
         tma_load_2d(dst + NB * 128, &xmap, (c_begin + i) * 128 + 64, 0, &full_b[s]);
@@ -579,6 +520,18 @@ cudaError_t launch_tc_t(const GemvParams& g, int S, bool pdl, cudaStream_t st) {
 }
 
 }  // namespace
+
+bool encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                          uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estride[2] = {1, 1};
+  return encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 int gemm_tc05_splits(int M, int N, int K, int G, int forced) {
   if (M < 1 || M > 64 || K % 128 || G % 128 || K % G) return 0;

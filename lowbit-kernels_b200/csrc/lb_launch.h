@@ -1,5 +1,6 @@
 // Host-side launch descriptors shared by the C-ABI layer and the kernel files.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -68,6 +69,10 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
                              __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,
                              int hd, int max_len, cudaStream_t st);
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st);
+
+// 2-D tiled tensor map (no interleave, L2 256-byte promotion, out-of-bound elements read as zero); false on failure
+bool encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                          uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 
 // tcgen05 skinny GEMM (lb_gemm_tc.cu), M <= 64: per 128-row tile a cluster of `splits` CTAs splitting K.
 // gemm_tc05_splits picks the split for a shape on the current device (forced > 0: that split, capped by the

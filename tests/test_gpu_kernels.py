@@ -162,7 +162,7 @@ def test_v6_gemv_parity(layers, name, m):
 
 @pytest.mark.parametrize("kernel", [0, 1, 2])
 @pytest.mark.parametrize("name", ["0.5b.kv", "1.5b.up", "3b.down", "odd_n", "tiny", "k128"])
-@pytest.mark.parametrize("m", [1, 7, 16, 24])
+@pytest.mark.parametrize("m", [1, 3, 7, 8, 16, 24])
 def test_every_gemv_kernel(layers, kernel, name, m):
     """Each kernel forced through the option against the oracle, whatever the dispatch would pick: automatic (0),
     the copy-ring GEMV (1) and the tcgen05 GEMM (2)."""
@@ -391,3 +391,4 @@ def test_no_kernel_wait_gave_up():
     """Every bounded wait in the kernels completed (the device error word is still zero)."""
     torch.cuda.synchronize()
     assert ops.ext().lib.lb_device_error() == 0
+
