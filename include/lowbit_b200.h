@@ -143,6 +143,25 @@ LB_API int lb_decode_attention(const void* qkv, const void* bias, const float* i
                         int hd, int64_t max_len, lb_stream_t stream);
 LB_API int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream);
 
+/*
+ * lb_decode_attention without caller-owned scratch, for callers that cannot allocate device memory when they call
+ * it -- a host loop in plain C, or another runtime's decode step that has no device allocator or memory pool of
+ * its own to draw from -- and so cannot pass part_o / part_ml. No counterpart in the reference (its extension
+ * returns torch-allocated tensors and has no scratch at all).
+ *
+ * Same arguments and results as lb_decode_attention minus part_o and part_ml. The partials live in a scratch
+ * array inside the library: 262144 floats (1 MiB) per device. A call needs nh * lb_decode_attention_splits(max_len)
+ * * (hd + 2) floats of it (Qwen2.5-3B at a 1024-token cache: 16 * 16 * 130 = 33280); larger calls fail with
+ * LB_ERR_ARGUMENT and a message naming the sizes. Nothing in the scratch needs to start at zero: every partial the
+ * combine step reads is written first by the same call. The scratch is one per device and shared by every call on
+ * it: calls that can run at the same time (different streams, or host threads without ordering between them)
+ * race on it, so the caller must serialize them. The first call on each device resolves the scratch address with
+ * cudaGetSymbolAddress; make that first call outside any stream capture.
+ */
+LB_API int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos,
+                                void* k_cache, void* v_cache, void* out, int nh, int nkv, int hd, int64_t max_len,
+                                lb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -368,6 +368,35 @@ int lb_decode_attention(const void* qkv, const void* bias, const float* inv_freq
                   "decode_attention");
 }
 
+int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos,
+                                void* k_cache, void* v_cache, void* out, int nh, int nkv, int hd, int64_t max_len,
+                                lb_stream_t stream) {
+  if (!qkv || !inv_freq || !pos || !k_cache || !v_cache || !out) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  int rc = check_heads(nh, nkv, hd, max_len);
+  if (rc) return rc;
+  if (hd % 8) return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8", hd);
+  const size_t splits = (size_t)lb::attn_splits((int)max_len);
+  const size_t need = (size_t)nh * splits * (size_t)(hd + 2);
+  if (need > lb::kNoAllocScratchFloats)
+    return fail(LB_ERR_ARGUMENT,
+                "lb_decode_attention_noalloc needs %zu floats of scratch (%d heads x %zu splits x (%d + 2)); the "
+                "library holds %zu -- pass caller-owned scratch to lb_decode_attention instead",
+                need, nh, splits, hd, lb::kNoAllocScratchFloats);
+  if (lb::attn_smem_bytes(nh, nkv, hd) > 200 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
+  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "caches must be 16-byte aligned");
+  if ((rc = check_device())) return rc;
+  float* scratch = lb::noalloc_attn_scratch();
+  if (!scratch) return fail(LB_ERR_CUDA, "could not resolve the attention scratch on this device");
+  float* part_o = scratch;
+  float* part_ml = scratch + (size_t)nh * splits * hd;
+  return launched(lb::launch_attention(static_cast<const __half*>(qkv), static_cast<const __half*>(bias), inv_freq, pos,
+                                       static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), part_o, part_ml,
+                                       static_cast<__half*>(out), nh, nkv, hd, (int)max_len,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                  "decode_attention_noalloc");
+}
+
 int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {
   if (!gu || !a) return fail(LB_ERR_ARGUMENT, "null pointer argument");
   if (I <= 0 || I > (1 << 28)) return fail(LB_ERR_ARGUMENT, "bad size %lld", (long long)I);

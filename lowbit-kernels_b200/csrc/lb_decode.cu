@@ -7,6 +7,8 @@
 // rounding to fp16 per stored tensor.
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "lb_common.cuh"
 #include "lb_launch.h"
 
@@ -316,6 +318,27 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
   if (e != cudaSuccess) return e;
   return launch_pdl(attn_combine_kernel, dim3(nh), dim3(hd), 0, st, (const float*)part_o, (const float*)part_ml, out, nh,
                     nkv, hd, nsplit);
+}
+
+// Scratch of lb_decode_attention_noalloc: the split partials (part_o, then part_ml) of callers that cannot pass
+// their own. Nothing in it needs to start at zero -- each call writes every partial its combine step reads.
+static __device__ __align__(256) float g_attn_scratch[kNoAllocScratchFloats];
+
+float* noalloc_attn_scratch() {
+  static std::atomic<float*> addr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  float* p = addr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* sym = nullptr;
+    if (cudaGetSymbolAddress(&sym, g_attn_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    p = static_cast<float*>(sym);
+    addr[dev].store(p, std::memory_order_release);
+  }
+  return p;
 }
 
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st) {

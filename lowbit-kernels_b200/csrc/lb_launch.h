@@ -69,6 +69,9 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
                              __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,
                              int hd, int max_len, cudaStream_t st);
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st);
+// lb_decode_attention_noalloc: library-held scratch for the split partials (1 MiB per device)
+constexpr size_t kNoAllocScratchFloats = 262144;
+float* noalloc_attn_scratch();   // this device's scratch address (cudaGetSymbolAddress on first use), or null
 
 // 2-D tiled tensor map (no interleave, L2 256-byte promotion, out-of-bound elements read as zero); false on failure
 bool encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,

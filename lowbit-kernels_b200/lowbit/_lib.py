@@ -38,6 +38,7 @@ SIGNATURES = {
     "lb_decode_attention_splits": ([_I64], _I),
     "lb_decode_attention": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _P], _I),
     "lb_decode_silu_mul": ([_P, _P, _I64, _P], _I),
+    "lb_decode_attention_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _P], _I),
 }
 
 
