@@ -660,6 +660,27 @@ def run_tp_decode(args, rank, world, local):
     return line if rank == 0 else None
 
 
+def profile_sweep(passes=2):
+    """No timing: `passes` eager passes over the 21 config-1 projections, each pass on its own weight set (cold:
+    15 sets rotate as in the benchmark), for an ncu capture of one whole step's launches (-s 21 -c 21)."""
+    from lowbit import ops, quant
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    e = ops.ext()
+    e.set_option("pdl", 1)
+    e.set_option("early_weights", 1)
+    projs = projections()
+    set_bytes = sum(n * k // 2 + 2 * n * (k // GROUP) for _, _, k, n in projs)
+    sets = build_sets(ops, quant, device, -(-ROTATION_BYTES // set_bytes), seed=1234)
+    gen = torch.Generator(device=device).manual_seed(99)
+    xs = [torch.randn(1, k, device=device, generator=gen).half() for _, _, k, _ in projs]
+    for p in range(passes):
+        for x, wq in zip(xs, sets[p % len(sets)]):
+            ops.linear(x, wq)
+    torch.cuda.synchronize()
+    print(f"profile sweep: {passes} passes x {len(projs)} calls", file=sys.stderr)
+
+
 def profile_decode(steps=3, prompt_len=8):
     """No timing: the config-3 decoder (Qwen2.5-3B, INT4) with a short prompt, then a few graph steps, for an ncu
     launch list of whole decode steps."""
@@ -687,11 +708,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
+    ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",
                     help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
     if args.profile_decode:
         profile_decode()
+        return
+    if args.profile_sweep:
+        profile_sweep()
         return
     if args.profile_case:
         profile_case(*(int(v) for v in args.profile_case.split(",")))

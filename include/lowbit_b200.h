@@ -144,6 +144,21 @@ LB_API int lb_decode_attention(const void* qkv, const void* bias, const float* i
 LB_API int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream);
 
 /*
+ * The decode step's activation work folded into the INT4 GEMV that consumes it (M = 1, mma-layout W, K and the
+ * group size multiples of 128, K <= 16384: one CTA holds the whole row; larger K -> LB_ERR_UNSUPPORTED, see
+ * lb_decode_gemv_fusable). Same numerics as the separate kernels followed by lb_w4_gemv.
+ * lb_decode_norm_gemv:   y[n] = W * (norm_w * fp16((x + r) * rsqrt(mean((x + r)^2) + eps))); x + r is also written
+ *                        to x_out (r and x_out may be NULL; x_out must not alias x or r)
+ * lb_decode_swiglu_gemv: y[n] = W * (fp16(silu(gu[0:k])) * gu[k:2k])
+ * lb_decode_gemv_fusable: 1 when a [n, k] layer can take these entry points, else 0
+ */
+LB_API int lb_decode_gemv_fusable(int64_t n, int64_t k);
+LB_API int lb_decode_norm_gemv(const void* x, const void* r, const void* norm_w, void* x_out, float eps, const void* w,
+                        const void* scales, void* y, int64_t n, int64_t k, int64_t group, lb_stream_t stream);
+LB_API int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scales, void* y, int64_t n, int64_t k,
+                          int64_t group, lb_stream_t stream);
+
+/*
  * lb_decode_attention without caller-owned scratch, for callers that cannot allocate device memory when they call
  * it -- a host loop in plain C, or another runtime's decode step that has no device allocator or memory pool of
  * its own to draw from -- and so cannot pass part_o / part_ml. No counterpart in the reference (its extension

@@ -151,6 +151,26 @@ lb::OneshotConfig oneshot_config(int M, int N, int K) {
   return c;
 }
 
+// One-shot configuration for M = 1 with the whole K range in one CTA (the decode prologues need the full row):
+// warps as the sweep chose them, up to 16 when the row is long; invalid (warps = 0) beyond 16 warps x 8 chunks.
+lb::OneshotConfig unsplit_config(int N, int K) {
+  lb::OneshotConfig c{0, 0, 0, 0, g_opt[LB_OPT_PDL].load()};
+  const int kc = K >> 7;
+  int nw = N >= 4096 ? 8 : 16;
+  const int fw = g_opt[LB_OPT_GEMV_WARPS].load();
+  if (fw >= 1 && fw <= 16) nw = fw;
+  if ((kc + nw - 1) / nw > 8) nw = 16;
+  if (nw > kc) nw = kc;
+  const int per = (kc + nw - 1) / nw;
+  const int cpw = per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : 0;
+  if (cpw == 0 || lb::oneshot_smem_bytes(1, K, 1, nw, 1) > 200 * 1024) return c;
+  c.warps = nw;
+  c.cpw = cpw;
+  c.ksplit = 1;
+  c.rt = 1;
+  return c;
+}
+
 int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
                  int64_t group, cudaStream_t st) {
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
@@ -395,6 +415,45 @@ int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* 
                                        static_cast<__half*>(out), nh, nkv, hd, (int)max_len,
                                        reinterpret_cast<cudaStream_t>(stream)),
                   "decode_attention_noalloc");
+}
+
+static int decode_gemv(int pro, const void* x, const void* r, const void* norm_w, void* x_out, float eps, const void* w,
+                       const void* scales, void* y, int64_t n, int64_t k, int64_t group, lb_stream_t stream) {
+  int rc = check_common(x, w, scales, y, 1, n, k, group);
+  if (rc) return rc;
+  if (k % 128 || group % 128) return fail(LB_ERR_ARGUMENT, "the fused decode GEMV needs K and the group size to be multiples of 128");
+  if (pro == 1 && !norm_w) return fail(LB_ERR_ARGUMENT, "null norm weight");
+  if (((reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(norm_w) | reinterpret_cast<uintptr_t>(x_out)) &
+       15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "r, norm weight and x_out must be 16-byte aligned");
+  const lb::OneshotConfig c = unsplit_config((int)n, (int)k);
+  if (c.warps == 0)
+    return fail(LB_ERR_UNSUPPORTED, "K=%lld is too long for a fused decode GEMV (one CTA holds at most 16384)",
+                (long long)k);
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), 1, (int)n, (int)k, (int)group,
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
+                   (int)(group / 128)};
+  p.pro = pro;
+  p.pro_r = static_cast<const __half*>(r);
+  p.pro_w = static_cast<const __half*>(norm_w);
+  p.pro_out = static_cast<__half*>(x_out);
+  p.pro_eps = eps;
+  return launched(lb::launch_gemv_oneshot(p, c, reinterpret_cast<cudaStream_t>(stream)), "decode_gemv");
+}
+
+int lb_decode_gemv_fusable(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0 || k % 128 || n > (1 << 30) || k > (1 << 28)) return 0;
+  return unsplit_config((int)n, (int)k).warps > 0 ? 1 : 0;
+}
+
+int lb_decode_norm_gemv(const void* x, const void* r, const void* norm_w, void* x_out, float eps, const void* w,
+                        const void* scales, void* y, int64_t n, int64_t k, int64_t group, lb_stream_t stream) {
+  return decode_gemv(1, x, r, norm_w, x_out, eps, w, scales, y, n, k, group, stream);
+}
+
+int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scales, void* y, int64_t n, int64_t k, int64_t group,
+                          lb_stream_t stream) {
+  return decode_gemv(2, gu, nullptr, nullptr, nullptr, 0.f, w, scales, y, n, k, group, stream);
 }
 
 int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {

@@ -282,7 +282,23 @@ void clear_device_error() {
   cudaMemcpyToSymbol(g_device_status, &z, sizeof(int));
 }
 
-template <int MT, int RT, int CPW, bool EARLY>
+// fp32 sum over the CTA (every thread calls it; red: 32 floats of shared memory)
+__device__ __forceinline__ float cta_sum_f32(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const float t = lane < nw ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+template <int MT, int RT, int CPW, bool EARLY, int PRO = 0>
 __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
@@ -358,6 +374,67 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   }
   cp_async_wait<0>();
   __syncthreads();
+
+  if constexpr (PRO != 0) {
+    // activation prologue (M = 1, the CTA holds the whole row): the decode step's RMSNorm (with the residual add)
+    // or SwiGLU, applied to the staged row in place -- the same fp16 roundings as the standalone kernels
+    __shared__ float pro_red[32];
+    uint4* xs = reinterpret_cast<uint4*>(smem);
+    const int n8 = K / 8;
+    if constexpr (PRO == 1) {
+      float ss = 0.f;
+      for (int v = threadIdx.x; v < n8; v += blockDim.x) {
+        uint4 xv = xs[v];
+        __half2* xh = reinterpret_cast<__half2*>(&xv);
+        if (p.pro_r) {
+          const uint4 rv = ldg_cg_u4(p.pro_r + 8 * (size_t)v);
+          const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xh[j] = __hadd2(xh[j], rh[j]);
+          xs[v] = xv;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(xh[j]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+      const float inv = rsqrtf(cta_sum_f32(ss, pro_red) / (float)K + p.pro_eps);
+      for (int v = threadIdx.x; v < n8; v += blockDim.x) {
+        const uint4 xv = xs[v];
+        const uint4 wv = ldg_stream(reinterpret_cast<const uint4*>(p.pro_w) + v);
+        if (blockIdx.x == 0 && p.pro_out) reinterpret_cast<uint4*>(p.pro_out)[v] = xv;
+        const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+        const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(xh[j]);
+          oh[j] = __hmul2(wh[j], __floats2half2_rn(f.x * inv, f.y * inv));
+        }
+        xs[v] = o;
+      }
+    } else {
+      const __half* up = reinterpret_cast<const __half*>(p.x) + K;
+      for (int v = threadIdx.x; v < n8; v += blockDim.x) {
+        const uint4 gv = xs[v];
+        const uint4 uv = ldg_cg_u4(up + 8 * (size_t)v);
+        const __half* gh = reinterpret_cast<const __half*>(&gv);
+        const __half* uh = reinterpret_cast<const __half*>(&uv);
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float gf = __half2float(gh[j]);
+          const __half sg = __float2half_rn(gf / (1.f + expf(-gf)));
+          oh[j] = __float2half_rn(__half2float(sg) * __half2float(uh[j]));
+        }
+        xs[v] = o;
+      }
+    }
+    __syncthreads();
+  }
 
   float acc[RT][MT][4];
 #pragma unroll
@@ -468,10 +545,10 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   }
 }
 
-template <int MT, int RT, int CPW>
+template <int MT, int RT, int CPW, int PRO = 0>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
-  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true>
-                                            : gemv_oneshot_kernel<MT, RT, CPW, false>;
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true, PRO>
+                                            : gemv_oneshot_kernel<MT, RT, CPW, false, PRO>;
   const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps, RT);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -511,6 +588,15 @@ size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt) {
 
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
   const int mt = p.M <= 8 ? 1 : 2;
+  if (p.pro != 0) {   // decode-step prologues: M = 1, the whole K range in one CTA, one row tile
+    if (p.M != 1 || c.ksplit != 1 || c.rt != 1) return cudaErrorInvalidConfiguration;
+#define LB_ONESHOT_PRO(PRO_, CPW_) \
+    if (p.pro == PRO_ && c.cpw == CPW_) return launch_oneshot_t<1, 1, CPW_, PRO_>(p, c, st);
+    LB_ONESHOT_PRO(1, 2) LB_ONESHOT_PRO(1, 4) LB_ONESHOT_PRO(1, 8)
+    LB_ONESHOT_PRO(2, 2) LB_ONESHOT_PRO(2, 4) LB_ONESHOT_PRO(2, 8)
+#undef LB_ONESHOT_PRO
+    return cudaErrorInvalidConfiguration;
+  }
 #define LB_ONESHOT(MT_, RT_, CPW_) \
   if (mt == MT_ && c.rt == RT_ && c.cpw == CPW_) return launch_oneshot_t<MT_, RT_, CPW_>(p, c, st);
   LB_ONESHOT(1, 1, 2) LB_ONESHOT(1, 1, 4) LB_ONESHOT(1, 1, 8) LB_ONESHOT(1, 2, 2) LB_ONESHOT(1, 2, 4)

@@ -22,6 +22,14 @@ struct GemvParams {
   int wait_guard;  // always 1 (see pdl_wait_after_loads)
   int KG;          // K / G, groups per row
   int cpg;         // G / 128, 128-wide chunks per group (mma layout kernels)
+  // activation prologue of the one-shot GEMV (M = 1, K unsplit): 0 none; 1 x <- w * fp16((x + r) *
+  // rsqrt(mean((x + r)^2) + eps)) with x + r written to out by CTA 0 (r, out may be null); 2 x <- silu(x[0:K]) *
+  // x[K:2K] (x is a [gate | up] row of 2K values)
+  int pro = 0;
+  const __half* pro_r = nullptr;
+  const __half* pro_w = nullptr;
+  __half* pro_out = nullptr;
+  float pro_eps = 0.f;
 };
 
 struct GemvConfig {
@@ -43,7 +51,7 @@ struct OneshotConfig {
   int rt;      // 16-row tiles per CTA: 1 or 2
   int pdl;
 };
-cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
+cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);  // p.pro: M = 1, ksplit 1, rt 1
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt);
 
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up

@@ -139,13 +139,13 @@ def enable_decode_options():
 
 
 class Int4Decoder:
-    """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm, q|k|v GEMV, attention (bias +
-    RoPE + KV append + split attention, combine), o GEMV, residual + RMSNorm, gate|up GEMV, SiLU*up, down GEMV] ->
-    final RMSNorm ->
+    """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm + q|k|v GEMV, attention (bias +
+    RoPE + KV append + split attention, combine), o GEMV, residual + RMSNorm + gate|up GEMV, SiLU*up + down GEMV]
+    (the norms and SwiGLU folded into the GEMV prologues where one CTA holds the row) -> final RMSNorm ->
     fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
     projections) and frees its decoder layers."""
 
-    def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None):
+    def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None, fuse=()):
         from . import tp
         e = ops.ext()
         self.lib = e.lib
@@ -190,6 +190,13 @@ class Int4Decoder:
                     "v": torch.zeros(self.nkv, max_len, hd, dtype=torch.half, device=dev),
                 }
                 self.int4_bytes += sum(ly[k].nbytes() for k in ("qkv", "o", "gu", "down"))
+                # RMSNorm / SwiGLU folded into the GEMV that consumes them (`fuse`: which of q|k|v, gate|up, down)
+                # where one CTA holds the whole row. Off by default: measured on B200 (3B, batch 1, 512 context) every
+                # fusion is slower than the separate kernels (625 tok/s none, 598 q|k|v, 552 q|k|v + gate|up, 537
+                # all): each of the GEMV's CTAs redoes the row's work (1376 CTAs for gate|up), which costs more
+                # than one small launch under programmatic dependent launch
+                for kind in ("qkv", "gu", "down"):
+                    ly["fuse_" + kind] = kind in fuse and bool(self.lib.lb_decode_gemv_fusable(ly[kind].n, ly[kind].k))
                 self.layers.append(ly)
         model.model.layers = None          # the fp16 projections are no longer needed
         torch.cuda.empty_cache()
@@ -200,7 +207,8 @@ class Int4Decoder:
         self.inv_freq = (1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))).to(dev)
         self.tok = torch.zeros(1, dtype=torch.long, device=dev)
         self.pos = torch.zeros(1, dtype=torch.long, device=dev)
-        self.x = torch.zeros(self.H, dtype=torch.half, device=dev)
+        self.x = torch.zeros(self.H, dtype=torch.half, device=dev)     # residual stream (two buffers: a fused
+        self.x2 = torch.zeros(self.H, dtype=torch.half, device=dev)    # norm GEMV writes x + r to the other)
         self.h = torch.zeros(self.H, dtype=torch.half, device=dev)
         self.attn = torch.zeros(1, self.nh * hd, dtype=torch.half, device=dev)
         self.act = torch.zeros(1, self.I, dtype=torch.half, device=dev)
@@ -224,16 +232,30 @@ class Int4Decoder:
         """KV-cache bytes this rank reads per step at `context` cached tokens."""
         return 2 * len(self.layers) * self.nkv * self.hd * 2 * context
 
+    def _norm_gemv(self, x, r, ln, x_out, wq, st):
+        y = torch.empty(1, wq.n, dtype=torch.half, device=self.device)
+        self._ok(self.lib.lb_decode_norm_gemv(x.data_ptr(), None if r is None else r.data_ptr(), ln.data_ptr(),
+                                              None if x_out is None else x_out.data_ptr(), self.eps,
+                                              wq.packed_mma.data_ptr(), wq.scales.data_ptr(), y.data_ptr(), wq.n, wq.k,
+                                              wq.group, st))
+        return y
+
     def _step(self):
         L, st = self.lib, torch.cuda.current_stream(self.device).cuda_stream
         nh, nkv, hd, H = self.nh, self.nkv, self.hd, self.H
-        self._ok(L.lb_decode_embed(self.embed.data_ptr(), self.tok.data_ptr(), self.x.data_ptr(), H, st))
+        cur, other = self.x, self.x2
+        self._ok(L.lb_decode_embed(self.embed.data_ptr(), self.tok.data_ptr(), cur.data_ptr(), H, st))
         h2 = self.h.view(1, H)
         resid = None
         for ly in self.layers:
-            self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, ly["ln1"].data_ptr(), self.h.data_ptr(), H,
-                                         self.eps, st))
-            qkv = ops.gemv(h2, ly["qkv"], 6)
+            if ly["fuse_qkv"]:
+                qkv = self._norm_gemv(cur, resid, ly["ln1"], None if resid is None else other, ly["qkv"], st)
+                if resid is not None:
+                    cur, other = other, cur
+            else:
+                self._ok(L.lb_decode_rmsnorm(cur.data_ptr(), None if resid is None else resid.data_ptr(),
+                                             ly["ln1"].data_ptr(), self.h.data_ptr(), H, self.eps, st))
+                qkv = ops.gemv(h2, ly["qkv"], 6)
             self._ok(L.lb_decode_attention(qkv.data_ptr(), None if ly["bias"] is None else ly["bias"].data_ptr(),
                                            self.inv_freq.data_ptr(), self.pos.data_ptr(), ly["k"].data_ptr(),
                                            ly["v"].data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
@@ -241,15 +263,26 @@ class Int4Decoder:
             o = ops.gemv(self.attn, ly["o"], 6)
             if self.world > 1:
                 torch.distributed.all_reduce(o, group=self.pg)
-            self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), o.data_ptr(), ly["ln2"].data_ptr(), self.h.data_ptr(), H,
-                                         self.eps, st))
-            gu = ops.gemv(h2, ly["gu"], 6)
-            self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
-            d = ops.gemv(self.act, ly["down"], 6)
+            if ly["fuse_gu"]:
+                gu = self._norm_gemv(cur, o, ly["ln2"], other, ly["gu"], st)
+                cur, other = other, cur
+            else:
+                self._ok(L.lb_decode_rmsnorm(cur.data_ptr(), o.data_ptr(), ly["ln2"].data_ptr(), self.h.data_ptr(), H,
+                                             self.eps, st))
+                gu = ops.gemv(h2, ly["gu"], 6)
+            if ly["fuse_down"]:
+                wq = ly["down"]
+                d = torch.empty(1, wq.n, dtype=torch.half, device=self.device)
+                self._ok(L.lb_decode_swiglu_gemv(gu.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(),
+                                                 d.data_ptr(), wq.n, wq.k, wq.group, st))
+            else:
+                self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
+                d = ops.gemv(self.act, ly["down"], 6)
             if self.world > 1:
                 torch.distributed.all_reduce(d, group=self.pg)
-            resid = d.data_ptr()
-        self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), resid, self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))
+            resid = d
+        self._ok(L.lb_decode_rmsnorm(cur.data_ptr(), None if resid is None else resid.data_ptr(),
+                                     self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))
         self.logits = torch.nn.functional.linear(h2, self.head)
         if self.world == 1:
             self.tok.copy_(self.logits.argmax(-1))
@@ -265,7 +298,8 @@ class Int4Decoder:
 
     def launches_per_step(self):
         """Kernels of this library per step (the lm_head GEMV and the argmax are cuBLAS / torch)."""
-        return 1 + len(self.layers) * 9 + 1
+        per = sum(6 + (not ly["fuse_qkv"]) + (not ly["fuse_gu"]) + (not ly["fuse_down"]) for ly in self.layers)
+        return 1 + per + 1
 
     @torch.no_grad()
     def capture(self):

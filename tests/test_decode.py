@@ -144,3 +144,58 @@ def test_silu_mul_kernel():
     assert _lib().lb_decode_silu_mul(gu.data_ptr(), a.data_ptr(), I, _stream()) == 0
     want = torch.nn.functional.silu(gu[:I]) * gu[I:]
     assert torch.allclose(a.float(), want.float(), atol=1e-3, rtol=2e-3)
+
+
+def _w4(n, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return ops.W4Weight.from_float(torch.randn(n, k, device="cuda", generator=g) * 0.02, 128, ("mma",))
+
+
+@pytest.mark.parametrize("nk", [(2560, 2048), (22016, 2048), (896, 896)])
+@pytest.mark.parametrize("with_residual", [True, False])
+def test_norm_gemv_matches_rmsnorm_then_gemv(nk, with_residual):
+    n, k = nk
+    wq = _w4(n, k, n + k)
+    g = torch.Generator(device="cuda").manual_seed(k)
+    x = torch.randn(k, device="cuda", generator=g).half()
+    r = torch.randn(k, device="cuda", generator=g).half() if with_residual else None
+    ln = (1 + 0.1 * torch.randn(k, device="cuda", generator=g)).half()
+    x_out = torch.zeros_like(x)
+    y = torch.empty(1, n, device="cuda").half()
+    rc = _lib().lb_decode_norm_gemv(x.data_ptr(), None if r is None else r.data_ptr(), ln.data_ptr(),
+                                    x_out.data_ptr() if with_residual else None, 1e-6, wq.packed_mma.data_ptr(),
+                                    wq.scales.data_ptr(), y.data_ptr(), n, k, 128, _stream())
+    assert rc == 0, _lib().lb_last_error()
+    # the separate path: RMSNorm kernel (updates its own copy of x in place), then the GEMV
+    xs, h = x.clone(), torch.empty_like(x)
+    assert _lib().lb_decode_rmsnorm(xs.data_ptr(), None if r is None else r.data_ptr(), ln.data_ptr(), h.data_ptr(),
+                                    k, 1e-6, _stream()) == 0
+    want = ops.gemv(h.view(1, k), wq, 6)
+    torch.cuda.synchronize()
+    if with_residual:
+        assert torch.equal(x_out, xs)          # x + r, one fp16 rounding
+    # the sums of squares run in another order: normalized values may move by an fp16 ulp
+    rms = want.float().pow(2).mean().sqrt()
+    assert (y.float() - want.float()).abs().max() / rms < 2e-3
+
+
+@pytest.mark.parametrize("nk", [(2048, 11008), (896, 4864)])
+def test_swiglu_gemv_is_silu_mul_then_gemv(nk):
+    n, k = nk
+    wq = _w4(n, k, 7 * n + k)
+    g = torch.Generator(device="cuda").manual_seed(n)
+    gu = (2 * torch.randn(1, 2 * k, device="cuda", generator=g)).half()
+    y = torch.empty(1, n, device="cuda").half()
+    assert _lib().lb_decode_swiglu_gemv(gu.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(), y.data_ptr(),
+                                        n, k, 128, _stream()) == 0
+    a = torch.empty(1, k, device="cuda").half()
+    assert _lib().lb_decode_silu_mul(gu.data_ptr(), a.data_ptr(), k, _stream()) == 0
+    want = ops.gemv(a, wq, 6)
+    torch.cuda.synchronize()
+    assert torch.equal(y, want)
+
+
+def test_decode_gemv_fusable_rule():
+    assert _lib().lb_decode_gemv_fusable(2048, 11008) == 1      # 3B down: 86 chunks over 16 warps
+    assert _lib().lb_decode_gemv_fusable(3584, 18944) == 0      # 7B down on one GPU: longer than one CTA holds
+    assert _lib().lb_decode_gemv_fusable(3584, 9472) == 1       # the same at tensor-parallel degree 2
