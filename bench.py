@@ -603,7 +603,7 @@ def run_tp_decode(args, rank, world, local):
     steps, warm = min(args.steps, 256), min(args.warmup, 64)
     m = decode.build(decode.QWEN25_7B, seed=0, device=device)
     dec = decode.Int4Decoder(m, TP_CONTEXT + warm + steps + 16, world=world, rank=rank,
-                             pg=dist.group.WORLD if dist else None)
+                             pg=dist.group.WORLD if dist else None, allreduce=args.allreduce)
     del m
     torch.cuda.empty_cache()
     gen = torch.Generator().manual_seed(7)
@@ -642,7 +642,9 @@ def run_tp_decode(args, rank, world, local):
         "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
         "config": {"workload": "config 4: Qwen2.5-7B architecture, 28 layers, INT4 group-128, untied fp16 lm_head",
                    "model": "Qwen2.5-7B (random init)", "global_batch": 1, "seq_len": TP_CONTEXT,
-                   "parallelism": f"tp{world}: column q|k|v, gate|up; row o, down + NCCL allreduce; vocab lm_head"},
+                   "parallelism": f"tp{world}: column q|k|v, gate|up; row o, down + "
+                                  f"{'one-shot peer-memory' if args.allreduce == 'oneshot' else 'NCCL'} allreduce; "
+                                  "vocab lm_head"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_bytes_per_token_per_rank": per_rank,
@@ -707,6 +709,8 @@ def main():
     ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",
+                    help="config 4: row-parallel sums by the library's one-shot kernel or by NCCL")
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",

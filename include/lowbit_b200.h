@@ -153,6 +153,18 @@ LB_API int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t st
  * lb_decode_gemv_fusable: 1 when a [n, k] layer can take these entry points, else 0
  */
 LB_API int lb_decode_gemv_fusable(int64_t n, int64_t k);
+
+/*
+ * Tensor-parallel decode: in-place-capable sum allreduce of n fp16 values over `world` ranks, one kernel per call
+ * on each rank, through peer-mapped memory (NVLink). No counterpart in the reference (single GPU only).
+ * bufs: device array of `world` pointers, bufs[r] = rank r's peer-mapped buffer: 256 bytes of epoch flags (zero
+ * at setup) then two slots of `cap` fp16. epoch: this rank's uint32 device counter (zero at setup), advanced by
+ * each call. Every rank must make the same sequence of calls. A rank waits about a second for its peers, then
+ * records 2 in the device status word (lb_device_error) and gives up instead of hanging. out may alias in; n and
+ * cap are multiples of 8, in and out 16-byte aligned.
+ */
+LB_API int lb_tp_allreduce(const void* in, void* out, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch,
+                    int rank, int world, lb_stream_t stream);
 LB_API int lb_decode_norm_gemv(const void* x, const void* r, const void* norm_w, void* x_out, float eps, const void* w,
                         const void* scales, void* y, int64_t n, int64_t k, int64_t group, lb_stream_t stream);
 LB_API int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scales, void* y, int64_t n, int64_t k,

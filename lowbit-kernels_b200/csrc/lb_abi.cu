@@ -222,13 +222,15 @@ const char* lb_status_string(int status) {
 const char* lb_last_error(void) { return g_err; }
 
 int lb_device_error(void) {
-  const int a = lb::device_error();
-  return a ? a : lb::gemm_tc_device_error();
+  int a = lb::device_error();
+  if (!a) a = lb::gemm_tc_device_error();
+  return a ? a : lb::allreduce_device_error();
 }
 
 void lb_clear_device_error(void) {
   lb::clear_device_error();
   lb::gemm_tc_clear_device_error();
+  lb::allreduce_clear_device_error();
 }
 
 int lb_set_option(int option, int value) {
@@ -454,6 +456,24 @@ int lb_decode_norm_gemv(const void* x, const void* r, const void* norm_w, void* 
 int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scales, void* y, int64_t n, int64_t k, int64_t group,
                           lb_stream_t stream) {
   return decode_gemv(2, gu, nullptr, nullptr, nullptr, 0.f, w, scales, y, n, k, group, stream);
+}
+
+int lb_tp_allreduce(const void* in, void* out, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch, int rank,
+                    int world, lb_stream_t stream) {
+  if (!in || !out || !bufs || !epoch) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(LB_ERR_ARGUMENT, "rank %d of world %d (at most 64 ranks)", rank, world);
+  if (n <= 0 || cap < n || cap > (1 << 26)) return fail(LB_ERR_ARGUMENT, "n = %lld must fit the slot capacity %lld",
+                                                        (long long)n, (long long)cap);
+  if (n % 8 || cap % 8) return fail(LB_ERR_ARGUMENT, "n and the slot capacity must be multiples of 8");
+  if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "in and out must be 16-byte aligned");
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_allreduce_oneshot(static_cast<const __half*>(in), static_cast<__half*>(out), (int)n,
+                                               (int)cap, reinterpret_cast<uint8_t* const*>(bufs), epoch, rank, world,
+                                               reinterpret_cast<cudaStream_t>(stream)),
+                  "tp_allreduce");
 }
 
 int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {

@@ -115,6 +115,7 @@ namespace lb {
 // an error code in g_device_error (read by lb_device_error()) and gives up instead of hanging the GPU.
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrBarrierTimeout = 1;
+constexpr int kErrPeerTimeout = 2;    // a peer rank did not publish its epoch in time (allreduce)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

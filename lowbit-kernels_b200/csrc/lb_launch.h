@@ -77,6 +77,11 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
                              __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,
                              int hd, int max_len, cudaStream_t st);
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st);
+// one-shot allreduce over peer memory (lb_allreduce.cu)
+cudaError_t launch_allreduce_oneshot(const __half* in, __half* out, int n, int cap, uint8_t* const* bufs,
+                                     uint32_t* epoch, int rank, int world, cudaStream_t st);
+int allreduce_device_error();   // synchronizes
+void allreduce_clear_device_error();
 // lb_decode_attention_noalloc: library-held scratch for the split partials (1 MiB per device)
 constexpr size_t kNoAllocScratchFloats = 262144;
 float* noalloc_attn_scratch();   // this device's scratch address (cudaGetSymbolAddress on first use), or null

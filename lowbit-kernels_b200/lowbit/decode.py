@@ -145,7 +145,7 @@ class Int4Decoder:
     fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
     projections) and frees its decoder layers."""
 
-    def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None, fuse=()):
+    def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None, fuse=(), allreduce="oneshot"):
         from . import tp
         e = ops.ext()
         self.lib = e.lib
@@ -219,6 +219,13 @@ class Int4Decoder:
         self.part_ml = torch.zeros(self.nh * splits * 2, dtype=torch.float32, device=dev)
         self.logits = None
         self.graph = None
+        # row-parallel sums: the library's one-shot kernel over peer memory, or NCCL
+        self.allreduce = None
+        if world > 1:
+            if allreduce == "oneshot":
+                self.allreduce = tp.OneShotAllReduce(self.H, pg, dev)
+            else:
+                self.allreduce = lambda t: torch.distributed.all_reduce(t, group=pg)
 
     def _ok(self, rc):
         if rc:
@@ -262,7 +269,7 @@ class Int4Decoder:
                                            self.attn.data_ptr(), nh, nkv, hd, self.max_len, st))
             o = ops.gemv(self.attn, ly["o"], 6)
             if self.world > 1:
-                torch.distributed.all_reduce(o, group=self.pg)
+                self.allreduce(o)
             if ly["fuse_gu"]:
                 gu = self._norm_gemv(cur, o, ly["ln2"], other, ly["gu"], st)
                 cur, other = other, cur
@@ -279,7 +286,7 @@ class Int4Decoder:
                 self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
                 d = ops.gemv(self.act, ly["down"], 6)
             if self.world > 1:
-                torch.distributed.all_reduce(d, group=self.pg)
+                self.allreduce(d)
             resid = d
         self._ok(L.lb_decode_rmsnorm(cur.data_ptr(), None if resid is None else resid.data_ptr(),
                                      self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))

@@ -64,3 +64,44 @@ def shard_layer(w, p):
             "o": w["o"][:, qr].contiguous(),
             "gu": torch.cat([w["gate"][i0:i1], w["up"][i0:i1]], 0).contiguous(),
             "down": w["down"][:, i0:i1].contiguous()}
+
+
+class OneShotAllReduce:
+    """In-place sum allreduce of small fp16 tensors for tensor-parallel decode: the library's one-shot kernel
+    (lb_tp_allreduce: one launch per call on each rank, peer loads over NVLink, bounded waits) on peer-mapped
+    buffers that torch's symmetric memory allocates and exchanges (plumbing only)."""
+
+    FLAG_BYTES = 256
+
+    def __init__(self, cap, group, device):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        from . import ops
+        self.lib = ops.ext().lib
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 64:
+            raise ValueError("at most 64 ranks")
+        self.cap = (cap + 7) // 8 * 8
+        try:
+            symm.enable_symm_mem_for_group(group.group_name)
+        except Exception:   # noqa: BLE001 - newer torch enables groups on first use
+            pass
+        self.buf = symm.empty(self.FLAG_BYTES // 2 + 2 * self.cap, dtype=torch.half, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        handle = symm.rendezvous(self.buf, group)
+        off = self.buf.data_ptr() - handle.buffer_ptrs[self.rank]
+        self.ptrs = torch.tensor([p + off for p in handle.buffer_ptrs], dtype=torch.int64, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.handle = handle
+        dist.barrier(group)
+
+    def __call__(self, t):
+        import torch
+        rc = self.lib.lb_tp_allreduce(t.data_ptr(), t.data_ptr(), t.numel(), self.cap, self.ptrs.data_ptr(),
+                                      self.epoch.data_ptr(), self.rank, self.world,
+                                      torch.cuda.current_stream(t.device).cuda_stream)
+        if rc:
+            raise RuntimeError(self.lib.lb_last_error().decode())
+        return t

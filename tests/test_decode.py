@@ -199,3 +199,53 @@ def test_decode_gemv_fusable_rule():
     assert _lib().lb_decode_gemv_fusable(2048, 11008) == 1      # 3B down: 86 chunks over 16 warps
     assert _lib().lb_decode_gemv_fusable(3584, 18944) == 0      # 7B down on one GPU: longer than one CTA holds
     assert _lib().lb_decode_gemv_fusable(3584, 9472) == 1       # the same at tensor-parallel degree 2
+
+
+def _ar_call(lib, t, cap, bufs, epoch, rank, world):
+    return lib.lb_tp_allreduce(t.data_ptr(), t.data_ptr(), t.numel(), cap, bufs.data_ptr(), epoch.data_ptr(), rank,
+                               world, _stream())
+
+
+def test_tp_allreduce_single_rank_and_simulated_peer():
+    """world 1: the sum is the input; world 2 with the peer simulated on this GPU (its flag and slot written
+    beforehand): the kernel passes its wait and adds the two slots in rank order."""
+    lib, cap, n = _lib(), 4096, 3584
+    mine = torch.zeros(128 + 2 * cap, device="cuda").half()
+    peer = torch.zeros(128 + 2 * cap, device="cuda").half()
+    epoch = torch.zeros(1, device="cuda", dtype=torch.int32)
+    t = torch.randn(n, device="cuda").half()
+    t0 = t.clone()
+    bufs = torch.tensor([mine.data_ptr()], dtype=torch.int64, device="cuda")
+    assert _ar_call(lib, t, cap, bufs, epoch, 0, 1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(t, t0) and epoch.item() == 1
+    # world 2, epoch 1 -> 2: slot 0; the "peer" has published epoch 2 into this rank's flags[1]
+    epoch.zero_()
+    epoch += 1
+    other = torch.randn(n, device="cuda").half()
+    peer[128:128 + n] = other
+    mine.view(torch.int32)[1] = 2
+    bufs = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    assert _ar_call(lib, t, cap, bufs, epoch, 0, 2) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(t, (t0.float() + other.float()).half()) and epoch.item() == 2
+    assert lib.lb_device_error() == 0
+
+
+def test_tp_allreduce_wait_runs_out_and_reports():
+    """A peer that never publishes its epoch: the wait gives up after about a second, the status word reads 2 and
+    the epoch does not advance; the context stays usable."""
+    lib, cap, n = _lib(), 1024, 1000   # n, cap multiples of 8
+    mine = torch.zeros(128 + 2 * cap, device="cuda").half()
+    peer = torch.zeros(128 + 2 * cap, device="cuda").half()
+    epoch = torch.zeros(1, device="cuda", dtype=torch.int32)
+    bufs = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    t = torch.ones(n, device="cuda").half()
+    lib.lb_clear_device_error()
+    assert _ar_call(lib, t, cap, bufs, epoch, 0, 2) == 0
+    torch.cuda.synchronize()
+    assert lib.lb_device_error() == 2
+    assert epoch.item() == 0
+    lib.lb_clear_device_error()
+    assert lib.lb_device_error() == 0
+    assert torch.isfinite((t + 1).float()).all()     # the context still runs kernels

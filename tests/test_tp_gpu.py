@@ -68,3 +68,57 @@ def test_tp2_decoder_matches_single_gpu():
         assert results[f"err{r}"] < 2e-2, results[f"err{r}"]
         toks, ref_toks = results[f"toks{r}"]
         assert sum(a == b for a, b in zip(toks, ref_toks)) >= 5, (toks, ref_toks)
+
+
+def _ar_rank(rank, world, port, results):
+    from datetime import timedelta
+    import torch.distributed as dist
+    from lowbit import ops, tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        ar = tp.OneShotAllReduce(3584, dist.group.WORLD, dev)
+        ok = True
+        for call in range(5):   # epochs cycle through both slots
+            g = torch.Generator(device=dev).manual_seed(100 * call + rank)
+            t = torch.randn(3584, device=dev, generator=g).half()
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            want = torch.stack(parts).float().sum(0).half()   # rank order, fp32, one rounding
+            ar(t)
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(t, want)
+        # in a CUDA graph: replays advance the device epoch
+        x = torch.ones(3584, device=dev).half() * (rank + 1)
+        gph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            y = x.clone()
+            ar(y)
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(gph):
+            y = x.clone()
+            ar(y)
+        for _ in range(3):
+            gph.replay()
+        torch.cuda.synchronize()
+        ok = ok and torch.all(y == sum(range(1, world + 1))).item()
+        results[f"ok{rank}"] = bool(ok)
+        results[f"err{rank}"] = ops.ext().lib.lb_device_error()
+        del gph
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_oneshot_allreduce_matches_rank_ordered_sum():
+    world = 2
+    results = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_ar_rank, args=(world, _free_port(), results), nprocs=world, start_method="spawn")
+    for r in range(world):
+        assert results[f"ok{r}"] and results[f"err{r}"] == 0
