@@ -515,7 +515,7 @@ def run_decode(args, rank, world, local):
     decode.enable_decode_options()
     steps, warm = min(args.steps, 256), min(args.warmup, 64)
     m = decode.build(decode.QWEN25_3B, seed=rank)
-    dec = decode.Int4Decoder(m, DECODE_CONTEXT + warm + 2 * steps + 16)
+    dec = decode.Int4Decoder(m, DECODE_CONTEXT + warm + 2 * steps + 16, fuse=fuse_arg(args))
     int4_bytes = dec.int4_bytes
     gen = torch.Generator().manual_seed(7 + rank)
     prompt = torch.randint(0, m.config.vocab_size, (DECODE_CONTEXT,), generator=gen)
@@ -562,7 +562,7 @@ def run_decode(args, rank, world, local):
         "config": {"workload": "config 3: Qwen2.5-3B architecture, 36 layers, 252 INT4 projections, tied fp16 lm_head",
                    "model": "Qwen2.5-3B (random init)", "global_batch": world, "seq_len": DECODE_CONTEXT,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "weights 2 GB per token >> 126 MB L2"},
+                   "l2": "weights 2 GB per token >> 126 MB L2", "fuse": list(fuse_arg(args))},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_bytes_per_token": per_tok,
@@ -603,7 +603,7 @@ def run_tp_decode(args, rank, world, local):
     steps, warm = min(args.steps, 256), min(args.warmup, 64)
     m = decode.build(decode.QWEN25_7B, seed=0, device=device)
     dec = decode.Int4Decoder(m, TP_CONTEXT + warm + steps + 16, world=world, rank=rank,
-                             pg=dist.group.WORLD if dist else None, allreduce=args.allreduce)
+                             pg=dist.group.WORLD if dist else None, allreduce=args.allreduce, fuse=fuse_arg(args))
     del m
     torch.cuda.empty_cache()
     gen = torch.Generator().manual_seed(7)
@@ -644,7 +644,7 @@ def run_tp_decode(args, rank, world, local):
                    "model": "Qwen2.5-7B (random init)", "global_batch": 1, "seq_len": TP_CONTEXT,
                    "parallelism": f"tp{world}: column q|k|v, gate|up; row o, down + "
                                   f"{'one-shot peer-memory' if args.allreduce == 'oneshot' else 'NCCL'} allreduce; "
-                                  "vocab lm_head"},
+                                  "vocab lm_head", "fuse": list(fuse_arg(args))},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_bytes_per_token_per_rank": per_rank,
@@ -683,13 +683,18 @@ def profile_sweep(passes=2):
     print(f"profile sweep: {passes} passes x {len(projs)} calls", file=sys.stderr)
 
 
-def profile_decode(steps=3, prompt_len=8):
+def fuse_arg(args):
+    """--fuse: comma-separated kernel fusions of the decode step (Int4Decoder's `fuse`)."""
+    return tuple(f for f in getattr(args, "fuse", "").split(",") if f)
+
+
+def profile_decode(fuse=(), steps=3, prompt_len=8):
     """No timing: the config-3 decoder (Qwen2.5-3B, INT4) with a short prompt, then a few graph steps, for an ncu
     launch list of whole decode steps."""
     from lowbit import decode
     torch.cuda.set_device(0)
     decode.enable_decode_options()
-    dec = decode.Int4Decoder(decode.build(decode.QWEN25_3B, seed=0), 64)
+    dec = decode.Int4Decoder(decode.build(decode.QWEN25_3B, seed=0), 64, fuse=fuse)
     dec.prefill(torch.arange(prompt_len) * 9973 % 151936)
     for _ in range(steps):
         dec.step()
@@ -711,13 +716,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",
                     help="config 4: row-parallel sums by the library's one-shot kernel or by NCCL")
+    ap.add_argument("--fuse", default="",
+                    help="configs 3, 4: decode-step fusions, comma-separated: epilogue (norms and SwiGLU in the "
+                         "GEMV / allreduce epilogues) or any of qkv, gu, down (GEMV prologues)")
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",
                     help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
     if args.profile_decode:
-        profile_decode()
+        profile_decode(fuse_arg(args))
         return
     if args.profile_sweep:
         profile_sweep()

@@ -165,6 +165,29 @@ LB_API int lb_decode_gemv_fusable(int64_t n, int64_t k);
  */
 LB_API int lb_tp_allreduce(const void* in, void* out, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch,
                     int rank, int world, lb_stream_t stream);
+
+/*
+ * lb_tp_allreduce followed, in the same kernel, by the decode step's residual add and RMSNorm: x_res += sum of the
+ * ranks' `in`; h_out = norm_w * fp16(x_res * rsqrt(mean(x_res^2) + eps)). The sum itself is not stored.
+ */
+LB_API int lb_tp_allreduce_norm(const void* in, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch, int rank,
+                         int world, void* x_res, const void* norm_w, void* h_out, float eps, lb_stream_t stream);
+
+/*
+ * Decode GEMVs with the following step in their epilogue: M = 1, the kernel, K split and row tiling of lb_w4_gemv
+ * version 6 at M = 1 (so y has its bits), K a multiple of 128:
+ * lb_decode_gemv_swiglu:        W's rows interleave gate and up (row 2i = gate_i, row 2i + 1 = up_i, N % 16 == 0);
+ *                               a[i] = fp16(fp16(silu(fp16(gate_i))) * fp16(up_i)), N / 2 outputs -- the bits of
+ *                               lb_w4_gemv followed by lb_decode_silu_mul
+ * lb_decode_gemv_residual_norm: y = W x is stored; the last CTA to finish then adds y into x_res and writes h_out =
+ *                               norm_w * fp16(x_res * rsqrt(mean(x_res^2) + eps)). counter: a device int, zero before
+ *                               the first call, left zero by every call; calls that can overlap need distinct ones
+ */
+LB_API int lb_decode_gemv_swiglu(const void* x, const void* w, const void* scales, void* a, int64_t n, int64_t k,
+                          int64_t group, lb_stream_t stream);
+LB_API int lb_decode_gemv_residual_norm(const void* x, const void* w, const void* scales, void* y, int64_t n, int64_t k,
+                                 int64_t group, void* x_res, const void* norm_w, void* h_out, float eps, int* counter,
+                                 lb_stream_t stream);
 LB_API int lb_decode_norm_gemv(const void* x, const void* r, const void* norm_w, void* x_out, float eps, const void* w,
                         const void* scales, void* y, int64_t n, int64_t k, int64_t group, lb_stream_t stream);
 LB_API int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scales, void* y, int64_t n, int64_t k,

@@ -476,6 +476,69 @@ int lb_tp_allreduce(const void* in, void* out, int64_t n, int64_t cap, void* con
                   "tp_allreduce");
 }
 
+int lb_tp_allreduce_norm(const void* in, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch, int rank, int world,
+                         void* x_res, const void* norm_w, void* h_out, float eps, lb_stream_t stream) {
+  if (!in || !bufs || !epoch || !x_res || !norm_w || !h_out) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(LB_ERR_ARGUMENT, "rank %d of world %d (at most 64 ranks)", rank, world);
+  if (n <= 0 || cap < n || cap > (1 << 26) || n % 8 || cap % 8)
+    return fail(LB_ERR_ARGUMENT, "n = %lld must be a multiple of 8 within the slot capacity %lld", (long long)n,
+                (long long)cap);
+  if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(x_res) | reinterpret_cast<uintptr_t>(norm_w) |
+        reinterpret_cast<uintptr_t>(h_out)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "in, x_res, norm_w and h_out must be 16-byte aligned");
+  int rc = check_device();
+  if (rc) return rc;
+  return launched(lb::launch_allreduce_oneshot(static_cast<const __half*>(in), nullptr, (int)n, (int)cap,
+                                               reinterpret_cast<uint8_t* const*>(bufs), epoch, rank, world,
+                                               reinterpret_cast<cudaStream_t>(stream), static_cast<__half*>(x_res),
+                                               static_cast<const __half*>(norm_w), static_cast<__half*>(h_out), eps),
+                  "tp_allreduce_norm");
+}
+
+// the plain M = 1 GEMV's own configuration (the same kernel, split and tiling as lb_w4_gemv version 6), with an
+// epilogue
+static int epi_gemv(lb::GemvParams& p, int64_t n, int64_t k, int64_t group, lb_stream_t stream) {
+  int rc = check_common(p.x, p.w, p.s, p.y, 1, n, k, group);
+  if (rc) return rc;
+  if (k % 128 || group % 128)
+    return fail(LB_ERR_ARGUMENT, "the fused decode GEMV needs K and the group size to be multiples of 128");
+  const lb::OneshotConfig c = oneshot_config(1, (int)n, (int)k);
+  if (c.warps == 0)
+    return fail(LB_ERR_UNSUPPORTED, "K=%lld is too long for the one-shot GEMV", (long long)k);
+  return launched(lb::launch_gemv_oneshot(p, c, reinterpret_cast<cudaStream_t>(stream)), "decode_gemv");
+}
+
+int lb_decode_gemv_swiglu(const void* x, const void* w, const void* scales, void* a, int64_t n, int64_t k, int64_t group,
+                          lb_stream_t stream) {
+  if (n % 16) return fail(LB_ERR_ARGUMENT, "the interleaved gate|up layer needs N %% 16 == 0 (N = %lld)", (long long)n);
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(a), 1, (int)n, (int)k, (int)group,
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
+                   (int)(group / 128)};
+  p.epi = 1;
+  return epi_gemv(p, n, k, group, stream);
+}
+
+int lb_decode_gemv_residual_norm(const void* x, const void* w, const void* scales, void* y, int64_t n, int64_t k,
+                                 int64_t group, void* x_res, const void* norm_w, void* h_out, float eps, int* counter,
+                                 lb_stream_t stream) {
+  if (!x_res || !norm_w || !h_out || !counter) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (n % 8) return fail(LB_ERR_ARGUMENT, "N = %lld must be a multiple of 8", (long long)n);
+  if (((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_res) | reinterpret_cast<uintptr_t>(norm_w) |
+        reinterpret_cast<uintptr_t>(h_out)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "y, x_res, norm_w and h_out must be 16-byte aligned");
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), 1, (int)n, (int)k, (int)group,
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
+                   (int)(group / 128)};
+  p.epi = 2;
+  p.epi_counter = counter;
+  p.epi_x = static_cast<__half*>(x_res);
+  p.epi_w = static_cast<const __half*>(norm_w);
+  p.epi_h = static_cast<__half*>(h_out);
+  p.epi_eps = eps;
+  return epi_gemv(p, n, k, group, stream);
+}
+
 int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {
   if (!gu || !a) return fail(LB_ERR_ARGUMENT, "null pointer argument");
   if (I <= 0 || I > (1 << 28)) return fail(LB_ERR_ARGUMENT, "bad size %lld", (long long)I);

@@ -46,9 +46,13 @@ __device__ __forceinline__ uint4 ld_u4_volatile(const void* p) {
 
 // n % 8 == 0: every thread moves whole 16-byte pieces; the peers' pieces of a round are all requested before any
 // is added, so a call pays about one NVLink round trip
+// with x_res: the sum is also added into the residual stream x_res and the new row is normalized, h = norm_w *
+// fp16(x * rsqrt(mean(x^2) + eps)) -- the decode step's residual add + RMSNorm after a row-parallel projection
 __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __half* in, __half* out, int n, int cap,
                                                                       uint8_t* const* bufs, uint32_t* epoch_p,
-                                                                      int rank, int world) {
+                                                                      int rank, int world, __half* x_res,
+                                                                      const __half* norm_w, __half* h_out,
+                                                                      float eps) {
   constexpr int kRanksPerRound = 8;
   __shared__ int timed_out;
   __shared__ const uint8_t* src[64];
@@ -85,6 +89,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
     }
   }
   __syncthreads();
+  float ss_part = 0.f;
   for (int v = threadIdx.x; v < n8; v += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int r0 = 0; r0 < world; r0 += kRanksPerRound) {
@@ -109,7 +114,40 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
     __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
     for (int k = 0; k < 4; ++k) oh[k] = __floats2half2_rn(acc[2 * k], acc[2 * k + 1]);
-    reinterpret_cast<uint4*>(out)[v] = o;
+    if (out) reinterpret_cast<uint4*>(out)[v] = o;
+    if (x_res) {
+      uint4 xv = reinterpret_cast<const uint4*>(x_res)[v];
+      __half2* xh = reinterpret_cast<__half2*>(&xv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        xh[k] = __hadd2(xh[k], oh[k]);
+        const float2 f = __half22float2(xh[k]);
+        ss_part += f.x * f.x + f.y * f.y;
+      }
+      reinterpret_cast<uint4*>(x_res)[v] = xv;
+    }
+  }
+  if (x_res) {
+    __shared__ float red[32];
+    float v = warp_sum(ss_part);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = (threadIdx.x & 31) < (int)(blockDim.x >> 5) ? red[threadIdx.x & 31] : 0.f;
+    const float inv = rsqrtf(warp_sum(t) / (float)n + eps);
+    for (int i = threadIdx.x; i < n8; i += blockDim.x) {   // the same pieces this thread wrote above
+      const uint4 xv = reinterpret_cast<const uint4*>(x_res)[i];
+      const uint4 wv = reinterpret_cast<const uint4*>(norm_w)[i];
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      uint4 hv;
+      __half2* hh = reinterpret_cast<__half2*>(&hv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(xh[k]);
+        hh[k] = __hmul2(wh[k], __floats2half2_rn(f.x * inv, f.y * inv));
+      }
+      reinterpret_cast<uint4*>(h_out)[i] = hv;
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0 && !timed_out) *epoch_p = e;
@@ -118,7 +156,8 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
 }  // namespace
 
 cudaError_t launch_allreduce_oneshot(const __half* in, __half* out, int n, int cap, uint8_t* const* bufs,
-                                     uint32_t* epoch, int rank, int world, cudaStream_t st) {
+                                     uint32_t* epoch, int rank, int world, cudaStream_t st, __half* x_res,
+                                     const __half* norm_w, __half* h_out, float eps) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kArThreads);
@@ -128,7 +167,8 @@ cudaError_t launch_allreduce_oneshot(const __half* in, __half* out, int n, int c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, allreduce_oneshot_kernel, in, out, n, cap, bufs, epoch, rank, world);
+  return cudaLaunchKernelEx(&cfg, allreduce_oneshot_kernel, in, out, n, cap, bufs, epoch, rank, world, x_res, norm_w,
+                            h_out, eps);
 }
 
 int allreduce_device_error() {

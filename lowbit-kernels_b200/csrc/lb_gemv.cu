@@ -292,13 +292,21 @@ __device__ __forceinline__ float cta_sum_f32(float v, float* red) {
   return warp_sum(t);
 }
 
+// fetch-and-add with acquire-release semantics at GPU scope: publishes what this thread (and, after a bar.sync,
+// its CTA) wrote before it and makes visible what the earlier adders published
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(int* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
   uint4 v;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
 
-template <int MT, int RT, int CPW, bool EARLY, int PRO = 0>
+template <int MT, int RT, int CPW, bool EARLY, int PRO = 0, int EPI = 0>
 __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* const sw = reinterpret_cast<uint32_t*>(smem);
@@ -523,32 +531,114 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     for (int w = 0; w < NW; ++w) v += red[w * kTile + e];
     return v;
   };
-  if (nsplit == 1) {
-    for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, cta_sum(e));
+  // the finished tile: one CTA's warps summed (nsplit == 1), or, with K split over a cluster, each rank's sum
+  // written into its slot of rank 0's buffer (after a cluster barrier: the buffer follows rank 0's reduction area),
+  // a second barrier publishing the slots, and rank 0 adding them in rank order
+  float* part = red + NW * kTile;
+  if (nsplit > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    float* dst = cluster.map_shared_rank(part, 0) + split * kTile;
+    cluster.sync();
+    for (int e = threadIdx.x; e < kTile; e += blockDim.x) dst[e] = cta_sum(e);
+    cluster.sync();
+    if (split != 0) return;
+  }
+  auto tile_sum = [&](int e) {
+    if (nsplit == 1) return cta_sum(e);
+    float v = 0.f;
+    for (int r = 0; r < nsplit; ++r) v += part[r * kTile + e];
+    return v;
+  };
+  if constexpr (EPI == 1) {
+    // SwiGLU over interleaved rows (M = 1): element (i, lane) of row tile r holds row 16 r + q with q = lane / 4
+    // (i = 0) or 8 + lane / 4 (i = 2); thread j < 8 RT combines rows 2j (gate) and 2j + 1 (up) of the CTA's rows
+    // into output n0 / 2 + j, with the roundings of the separate GEMV and SiLU*up kernels
+    if (threadIdx.x < 8 * RT) {
+      const int j = threadIdx.x, r = j >> 3, rg = 2 * (j & 7), ru = rg + 1;
+      const int base = r * MT * 128;
+      const float gv = tile_sum(base + (rg < 8 ? 0 : 64) + 4 * (rg & 7));
+      const float uv = tile_sum(base + (ru < 8 ? 0 : 64) + 4 * (ru & 7));
+      const float gf = __half2float(__float2half_rn(gv));
+      const __half sg = __float2half_rn(gf / (1.f + expf(-gf)));
+      if (n0 + 16 * r + ru < N) p.y[n0 / 2 + j] = __float2half_rn(__half2float(sg) * __half2float(__float2half_rn(uv)));
+    }
     return;
   }
-  // cluster split-K: each rank writes its partial tiles into its slot of rank 0's buffer (after a cluster
-  // barrier: the buffer follows rank 0's reduction area), a second barrier publishes the slots, rank 0 adds
-  // them in rank order
-  cg::cluster_group cluster = cg::this_cluster();
-  float* part = red + NW * kTile;
-  float* dst = cluster.map_shared_rank(part, 0) + split * kTile;
-  cluster.sync();
-  for (int e = threadIdx.x; e < kTile; e += blockDim.x) dst[e] = cta_sum(e);
-  cluster.sync();
-  if (split == 0) {
-    for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
-      float v = 0.f;
-      for (int r = 0; r < nsplit; ++r) v += part[r * kTile + e];
-      store(e, v);
+  for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, tile_sum(e));
+  if constexpr (EPI == 2) {
+    // the last row tile to finish adds the whole output row into the residual stream and normalizes it (the
+    // counter counts the tiles' finishing CTAs -- rank 0 of each cluster -- and is left zero for the next call).
+    // Every such CTA first loads its pieces of the residual row and the norm weights (neither is written by this
+    // kernel before the count completes), so the last one starts its reduction with only y still to read.
+    constexpr int kPre = 4;   // pieces held per thread: N <= 8 * kPre * blockDim covers N <= 8192 at 256 threads
+    __shared__ int last;
+    __shared__ float epi_red[32];
+    const int n8 = N / 8;
+    uint4 xpre[kPre], wpre[kPre];
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int v = threadIdx.x + j * blockDim.x;
+      if (v < n8) {
+        xpre[j] = ldg_cg_u4(p.epi_x + 8 * (size_t)v);
+        wpre[j] = ldg_stream(reinterpret_cast<const uint4*>(p.epi_w) + v);
+      }
     }
+    __syncthreads();   // this CTA's y stores precede thread 0's release below (bar.sync, then a cumulative release)
+    if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(p.epi_counter, 1) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    float ss = 0.f;
+    auto add_piece = [&](int v, uint4& xv) {
+      const uint4 yv = ldg_cg_u4(p.y + 8 * (size_t)v);
+      __half2* xh = reinterpret_cast<__half2*>(&xv);
+      const __half2* yh = reinterpret_cast<const __half2*>(&yv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xh[j] = __hadd2(xh[j], yh[j]);
+        const float2 f = __half22float2(xh[j]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+      reinterpret_cast<uint4*>(p.epi_x)[v] = xv;
+    };
+    auto norm_piece = [&](int v, const uint4& xv, const uint4& wv, float inv) {
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(xh[j]);
+        oh[j] = __hmul2(wh[j], __floats2half2_rn(f.x * inv, f.y * inv));
+      }
+      reinterpret_cast<uint4*>(p.epi_h)[v] = o;
+    };
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int v = threadIdx.x + j * blockDim.x;
+      if (v < n8) add_piece(v, xpre[j]);
+    }
+    for (int v = threadIdx.x + kPre * blockDim.x; v < n8; v += blockDim.x) {   // rows longer than the registers hold
+      uint4 xv = ldg_cg_u4(p.epi_x + 8 * (size_t)v);
+      add_piece(v, xv);
+    }
+    const float inv = rsqrtf(cta_sum_f32(ss, epi_red) / (float)N + p.epi_eps);
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int v = threadIdx.x + j * blockDim.x;
+      if (v < n8) norm_piece(v, xpre[j], wpre[j], inv);
+    }
+    for (int v = threadIdx.x + kPre * blockDim.x; v < n8; v += blockDim.x) {   // this thread's own writes above
+      const uint4 xv = reinterpret_cast<const uint4*>(p.epi_x)[v];
+      norm_piece(v, xv, ldg_stream(reinterpret_cast<const uint4*>(p.epi_w) + v), inv);
+    }
+    if (threadIdx.x == 0) *p.epi_counter = 0;
   }
 }
 
-template <int MT, int RT, int CPW, int PRO = 0>
+template <int MT, int RT, int CPW, int PRO = 0, int EPI = 0>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
-  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true, PRO>
-                                            : gemv_oneshot_kernel<MT, RT, CPW, false, PRO>;
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true, PRO, EPI>
+                                            : gemv_oneshot_kernel<MT, RT, CPW, false, PRO, EPI>;
   const size_t smem = oneshot_smem_bytes(p.M, p.K, c.ksplit, c.warps, RT);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -588,6 +678,16 @@ size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt) {
 
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
   const int mt = p.M <= 8 ? 1 : 2;
+  if (p.epi != 0) {   // decode-step epilogues: M = 1, any K split and row tiling of the plain GEMV
+    if (p.M != 1 || p.pro != 0) return cudaErrorInvalidConfiguration;
+#define LB_ONESHOT_EPI(EPI_, RT_, CPW_) \
+    if (p.epi == EPI_ && c.rt == RT_ && c.cpw == CPW_) return launch_oneshot_t<1, RT_, CPW_, 0, EPI_>(p, c, st);
+    LB_ONESHOT_EPI(1, 1, 2) LB_ONESHOT_EPI(1, 1, 4) LB_ONESHOT_EPI(1, 1, 8) LB_ONESHOT_EPI(1, 2, 2)
+    LB_ONESHOT_EPI(1, 2, 4) LB_ONESHOT_EPI(2, 1, 2) LB_ONESHOT_EPI(2, 1, 4) LB_ONESHOT_EPI(2, 1, 8)
+    LB_ONESHOT_EPI(2, 2, 2) LB_ONESHOT_EPI(2, 2, 4)
+#undef LB_ONESHOT_EPI
+    return cudaErrorInvalidConfiguration;
+  }
   if (p.pro != 0) {   // decode-step prologues: M = 1, the whole K range in one CTA, one row tile
     if (p.M != 1 || c.ksplit != 1 || c.rt != 1) return cudaErrorInvalidConfiguration;
 #define LB_ONESHOT_PRO(PRO_, CPW_) \

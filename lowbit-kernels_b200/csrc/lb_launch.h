@@ -30,6 +30,16 @@ struct GemvParams {
   const __half* pro_w = nullptr;
   __half* pro_out = nullptr;
   float pro_eps = 0.f;
+  // output epilogue of the one-shot GEMV (M = 1, K unsplit, one row tile): 0 none; 1 SwiGLU over interleaved rows
+  // (W rows 2i, 2i + 1 = gate_i, up_i): y[i] = fp16(fp16(silu(fp16(gate_i))) * fp16(up_i)), N / 2 outputs; 2 y is
+  // stored, then the last CTA to finish (epi_counter, zero between calls) adds y into the residual stream epi_x
+  // and writes epi_h = epi_w * fp16(x * rsqrt(mean(x^2) + eps)) for the next projection
+  int epi = 0;
+  int* epi_counter = nullptr;
+  __half* epi_x = nullptr;
+  const __half* epi_w = nullptr;
+  __half* epi_h = nullptr;
+  float epi_eps = 0.f;
 };
 
 struct GemvConfig {
@@ -51,7 +61,7 @@ struct OneshotConfig {
   int rt;      // 16-row tiles per CTA: 1 or 2
   int pdl;
 };
-cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);  // p.pro: M = 1, ksplit 1, rt 1
+cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);  // p.pro / p.epi: M = 1, ksplit 1, rt 1
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt);
 
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
@@ -79,7 +89,8 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
 cudaError_t launch_silu_mul(const __half* gu, __half* a, int I, cudaStream_t st);
 // one-shot allreduce over peer memory (lb_allreduce.cu)
 cudaError_t launch_allreduce_oneshot(const __half* in, __half* out, int n, int cap, uint8_t* const* bufs,
-                                     uint32_t* epoch, int rank, int world, cudaStream_t st);
+                                     uint32_t* epoch, int rank, int world, cudaStream_t st, __half* x_res = nullptr,
+                                     const __half* norm_w = nullptr, __half* h_out = nullptr, float eps = 0.f);
 int allreduce_device_error();   // synchronizes
 void allreduce_clear_device_error();
 // lb_decode_attention_noalloc: library-held scratch for the split partials (1 MiB per device)

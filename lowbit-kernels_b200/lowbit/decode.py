@@ -14,7 +14,7 @@ transformers 5.5 a captured transformers step replays wrong logits for the fp16 
 import torch
 
 from . import model as lbm
-from . import ops
+from . import ops, tp
 
 # Qwen2.5 architectures of the benchmark configs (head_dim 128, RMSNorm eps 1e-6, RoPE theta 1e6, SwiGLU)
 QWEN25_3B = dict(hidden_size=2048, intermediate_size=11008, num_hidden_layers=36, num_attention_heads=16,
@@ -141,12 +141,16 @@ def enable_decode_options():
 class Int4Decoder:
     """Qwen2 decode step on the library's kernels: embed -> per layer [RMSNorm + q|k|v GEMV, attention (bias +
     RoPE + KV append + split attention, combine), o GEMV, residual + RMSNorm + gate|up GEMV, SiLU*up + down GEMV]
-    (the norms and SwiGLU folded into the GEMV prologues where one CTA holds the row) -> final RMSNorm ->
-    fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM (fp16, nn.Linear
-    projections) and frees its decoder layers."""
+    -> final RMSNorm -> fp16 lm_head (cuBLAS) -> argmax. Takes the weights of a transformers Qwen2ForCausalLM
+    (fp16, nn.Linear projections) and frees its decoder layers.
+
+    `fuse` picks kernel fusions: "norm_epilogue" ends the o and down GEMVs with the residual add + next RMSNorm
+    (the last CTA of the GEMV, or the one-shot allreduce under tensor parallelism); "swiglu_epilogue" ends the
+    gate|up GEMV with SiLU*up (its rows interleaved); "epilogue" is both, so a layer is q|k|v GEMV, attention, o,
+    gate|up, down. "qkv", "gu", "down" instead fold the preceding norm or SwiGLU into the GEMV's prologue where
+    one CTA holds the row."""
 
     def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None, fuse=(), allreduce="oneshot"):
-        from . import tp
         e = ops.ext()
         self.lib = e.lib
         cfg = model.config
@@ -156,6 +160,9 @@ class Int4Decoder:
         self.eps = float(cfg.rms_norm_eps)
         self.max_len = max_len
         self.world, self.rank, self.pg = world, rank, pg
+        self.epi_norm = "epilogue" in fuse or "norm_epilogue" in fuse
+        self.epi_swiglu = "epilogue" in fuse or "swiglu_epilogue" in fuse
+        self.epilogue = self.epi_norm or self.epi_swiglu
         theta = float(cfg.rope_parameters["rope_theta"])
         dev = model.model.embed_tokens.weight.device
         self.device = dev
@@ -177,7 +184,7 @@ class Int4Decoder:
                 w = {"q": a.q_proj.weight, "k": a.k_proj.weight, "v": a.v_proj.weight, "o": a.o_proj.weight,
                      "gate": m.gate_proj.weight, "up": m.up_proj.weight, "down": m.down_proj.weight,
                      "q_b": a.q_proj.bias, "k_b": a.k_proj.bias, "v_b": a.v_proj.bias}
-                sh = tp.shard_layer(w, shard)
+                sh = tp.shard_layer(w, shard, interleave=self.epi_swiglu)
                 ly = {
                     "qkv": w4(sh["qkv"]),
                     "bias": None if sh["bias"] is None else sh["bias"].half().contiguous(),
@@ -196,7 +203,8 @@ class Int4Decoder:
                 # all): each of the GEMV's CTAs redoes the row's work (1376 CTAs for gate|up), which costs more
                 # than one small launch under programmatic dependent launch
                 for kind in ("qkv", "gu", "down"):
-                    ly["fuse_" + kind] = kind in fuse and bool(self.lib.lb_decode_gemv_fusable(ly[kind].n, ly[kind].k))
+                    ly["fuse_" + kind] = (not self.epilogue and kind in fuse
+                                          and bool(self.lib.lb_decode_gemv_fusable(ly[kind].n, ly[kind].k)))
                 self.layers.append(ly)
         model.model.layers = None          # the fp16 projections are no longer needed
         torch.cuda.empty_cache()
@@ -212,6 +220,7 @@ class Int4Decoder:
         self.h = torch.zeros(self.H, dtype=torch.half, device=dev)
         self.attn = torch.zeros(1, self.nh * hd, dtype=torch.half, device=dev)
         self.act = torch.zeros(1, self.I, dtype=torch.half, device=dev)
+        self.counters = torch.zeros(2, dtype=torch.int32, device=dev)   # last-CTA counters of the o, down GEMVs
         self.pair = torch.zeros(2, dtype=torch.float32, device=dev)
         self.pairs = torch.zeros(2 * world, dtype=torch.float32, device=dev)
         splits = self.lib.lb_decode_attention_splits(max_len)
@@ -247,7 +256,69 @@ class Int4Decoder:
                                               wq.group, st))
         return y
 
+    def _residual_gemv(self, x, wq, ln, slot, st):
+        """y = W x (row-parallel under tensor parallelism: summed over the ranks), then the residual stream
+        self.x += y and self.h = RMSNorm(self.x) * ln -- in the GEMV's or the allreduce's epilogue with
+        "norm_epilogue", else by the RMSNorm kernel."""
+        y = torch.empty(1, wq.n, dtype=torch.half, device=self.device)
+        if self.world == 1 and self.epi_norm:
+            self._ok(self.lib.lb_decode_gemv_residual_norm(
+                x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(), y.data_ptr(), wq.n, wq.k, wq.group,
+                self.x.data_ptr(), ln.data_ptr(), self.h.data_ptr(), self.eps, self.counters.data_ptr() + 4 * slot,
+                st))
+            return
+        y = ops.gemv(x, wq, 6)
+        if self.epi_norm and isinstance(self.allreduce, tp.OneShotAllReduce):
+            self.allreduce.residual_norm(y, self.x, ln, self.h, self.eps)
+        else:
+            if self.world > 1:
+                self.allreduce(y)
+            self._ok(self.lib.lb_decode_rmsnorm(self.x.data_ptr(), y.data_ptr(), ln.data_ptr(), self.h.data_ptr(),
+                                                self.H, self.eps, st))
+
+    def _step_epilogue(self):
+        L, st = self.lib, torch.cuda.current_stream(self.device).cuda_stream
+        nh, nkv, hd, H = self.nh, self.nkv, self.hd, self.H
+        self._ok(L.lb_decode_embed(self.embed.data_ptr(), self.tok.data_ptr(), self.x.data_ptr(), H, st))
+        self._ok(L.lb_decode_rmsnorm(self.x.data_ptr(), None, self.layers[0]["ln1"].data_ptr(), self.h.data_ptr(), H,
+                                     self.eps, st))
+        h2 = self.h.view(1, H)
+        for i, ly in enumerate(self.layers):
+            qkv = ops.gemv(h2, ly["qkv"], 6)
+            self._ok(L.lb_decode_attention(qkv.data_ptr(), None if ly["bias"] is None else ly["bias"].data_ptr(),
+                                           self.inv_freq.data_ptr(), self.pos.data_ptr(), ly["k"].data_ptr(),
+                                           ly["v"].data_ptr(), self.part_o.data_ptr(), self.part_ml.data_ptr(),
+                                           self.attn.data_ptr(), nh, nkv, hd, self.max_len, st))
+            self._residual_gemv(self.attn, ly["o"], ly["ln2"], 0, st)
+            wq = ly["gu"]
+            if self.epi_swiglu:
+                self._ok(L.lb_decode_gemv_swiglu(self.h.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(),
+                                                 self.act.data_ptr(), wq.n, wq.k, wq.group, st))
+            else:
+                gu = ops.gemv(h2, wq, 6)
+                self._ok(L.lb_decode_silu_mul(gu.data_ptr(), self.act.data_ptr(), self.I, st))
+            nxt = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else self.norm
+            self._residual_gemv(self.act, ly["down"], nxt, 1, st)
+        self._head()
+
+    def _head(self):
+        h2 = self.h.view(1, self.H)
+        self.logits = torch.nn.functional.linear(h2, self.head)
+        if self.world == 1:
+            self.tok.copy_(self.logits.argmax(-1))
+        else:
+            # vocabulary-parallel argmax: each rank's best (value, global index); the first rank holding the
+            # overall maximum wins, which is the first occurrence over the whole vocabulary
+            val, idx = self.logits.float().max(-1)
+            self.pair.copy_(torch.cat([val, (idx + self.vocab0).float()]))
+            torch.distributed.all_gather_into_tensor(self.pairs, self.pair, group=self.pg)
+            pr = self.pairs.view(self.world, 2)
+            self.tok.copy_(pr[:, 1].gather(0, pr[:, 0].argmax().view(1)).long())   # no host sync
+        self.pos.add_(1)
+
     def _step(self):
+        if self.epilogue:
+            return self._step_epilogue()
         L, st = self.lib, torch.cuda.current_stream(self.device).cuda_stream
         nh, nkv, hd, H = self.nh, self.nkv, self.hd, self.H
         cur, other = self.x, self.x2
@@ -290,22 +361,18 @@ class Int4Decoder:
             resid = d
         self._ok(L.lb_decode_rmsnorm(cur.data_ptr(), None if resid is None else resid.data_ptr(),
                                      self.norm.data_ptr(), self.h.data_ptr(), H, self.eps, st))
-        self.logits = torch.nn.functional.linear(h2, self.head)
-        if self.world == 1:
-            self.tok.copy_(self.logits.argmax(-1))
-        else:
-            # vocabulary-parallel argmax: each rank's best (value, global index); the first rank holding the
-            # overall maximum wins, which is the first occurrence over the whole vocabulary
-            val, idx = self.logits.float().max(-1)
-            self.pair.copy_(torch.cat([val, (idx + self.vocab0).float()]))
-            torch.distributed.all_gather_into_tensor(self.pairs, self.pair, group=self.pg)
-            pr = self.pairs.view(self.world, 2)
-            self.tok.copy_(pr[:, 1].gather(0, pr[:, 0].argmax().view(1)).long())   # no host sync
-        self.pos.add_(1)
+        self._head()
 
     def launches_per_step(self):
-        """Kernels of this library per step (the lm_head GEMV and the argmax are cuBLAS / torch)."""
-        per = sum(6 + (not ly["fuse_qkv"]) + (not ly["fuse_gu"]) + (not ly["fuse_down"]) for ly in self.layers)
+        """Kernels of this library per step (the lm_head GEMV, the argmax and NCCL are not counted)."""
+        oneshot = 2 * isinstance(self.allreduce, tp.OneShotAllReduce)   # the o and down allreduces of a layer
+        if self.epilogue:   # q|k|v, attention (2), o, gate|up, down + the unfused norms and SiLU*up
+            norms = 0 if self.epi_norm and (self.world == 1 or oneshot) else 2
+            ar = oneshot if self.world > 1 else 0
+            per = 6 + ar + norms + (not self.epi_swiglu)
+            return 2 + per * len(self.layers)
+        per = sum(6 + oneshot + (not ly["fuse_qkv"]) + (not ly["fuse_gu"]) + (not ly["fuse_down"])
+                  for ly in self.layers)
         return 1 + per + 1
 
     @torch.no_grad()

@@ -48,10 +48,12 @@ def plan(nh, nkv, hd, inter, vocab, world, rank):
             "vocab": even_split(vocab, world)[rank], "hd": hd}
 
 
-def shard_layer(w, p):
+def shard_layer(w, p, interleave=False):
     """Slice one decoder layer's fp16 weights (dict of torch tensors: q, k, v, o, gate, up, down weights and
     q_b, k_b, v_b biases, nn.Linear [out, in] layout) to the shard `p`. Returns the fused q|k|v rows (+ bias),
-    the o columns, the fused gate|up rows and the down columns."""
+    the o columns, the fused gate|up rows -- [gate; up], or with `interleave` gate_0, up_0, gate_1, up_1, ...
+    (the layout of the SwiGLU-epilogue GEMV) -- and the down columns. Quantization is per row, so either order
+    holds the same quantized rows."""
     import torch
     hd = p["hd"]
     q0, q1 = p["q_heads"]
@@ -62,7 +64,8 @@ def shard_layer(w, p):
     bias = None if w.get("q_b") is None else torch.cat([w["q_b"][qr], w["k_b"][kr], w["v_b"][kr]], 0)
     return {"qkv": qkv.contiguous(), "bias": bias,
             "o": w["o"][:, qr].contiguous(),
-            "gu": torch.cat([w["gate"][i0:i1], w["up"][i0:i1]], 0).contiguous(),
+            "gu": (torch.stack([w["gate"][i0:i1], w["up"][i0:i1]], 1).reshape(2 * (i1 - i0), -1) if interleave
+                   else torch.cat([w["gate"][i0:i1], w["up"][i0:i1]], 0)).contiguous(),
             "down": w["down"][:, i0:i1].contiguous()}
 
 
@@ -105,3 +108,14 @@ class OneShotAllReduce:
         if rc:
             raise RuntimeError(self.lib.lb_last_error().decode())
         return t
+
+    def residual_norm(self, t, x_res, norm_w, h, eps):
+        """x_res += the sum of every rank's t; h = RMSNorm(x_res) * norm_w (lb_tp_allreduce_norm, one launch);
+        t is left as it was."""
+        import torch
+        rc = self.lib.lb_tp_allreduce_norm(t.data_ptr(), t.numel(), self.cap, self.ptrs.data_ptr(),
+                                           self.epoch.data_ptr(), self.rank, self.world, x_res.data_ptr(),
+                                           norm_w.data_ptr(), h.data_ptr(), eps,
+                                           torch.cuda.current_stream(t.device).cuda_stream)
+        if rc:
+            raise RuntimeError(self.lib.lb_last_error().decode())

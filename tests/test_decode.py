@@ -15,13 +15,14 @@ TINY = dict(hidden_size=256, intermediate_size=640, num_hidden_layers=2, num_att
 
 
 @torch.no_grad()
-def test_int4_decoder_matches_fake_quant_and_replays_bit_exactly():
+@pytest.mark.parametrize("fuse", [(), ("epilogue",)])
+def test_int4_decoder_matches_fake_quant_and_replays_bit_exactly(fuse):
     decode.enable_decode_options()
     gen = torch.Generator().manual_seed(1)
     prompt = torch.randint(0, TINY["vocab_size"], (24,), generator=gen)
     seq = torch.randint(0, TINY["vocab_size"], (12,), generator=gen).tolist()
 
-    dec = decode.Int4Decoder(decode.build(TINY, seed=3), max_len=64)
+    dec = decode.Int4Decoder(decode.build(TINY, seed=3), max_len=64, fuse=fuse)
     assert dec.int4_bytes > 0
     first = dec.prefill(prompt).float()
     got = dec.forced(seq)
@@ -52,10 +53,11 @@ def test_int4_decoder_matches_fake_quant_and_replays_bit_exactly():
 
 
 @torch.no_grad()
-def test_greedy_continuation_is_the_argmax():
+@pytest.mark.parametrize("fuse", [(), ("epilogue",)])
+def test_greedy_continuation_is_the_argmax(fuse):
     """Free-running decode: each step's token is the argmax of that step's logits."""
     decode.enable_decode_options()
-    dec = decode.Int4Decoder(decode.build(TINY, seed=5), max_len=48)
+    dec = decode.Int4Decoder(decode.build(TINY, seed=5), max_len=48, fuse=fuse)
     dec.prefill(torch.arange(16) * 37 % TINY["vocab_size"])
     for _ in range(8):
         dec.step()
@@ -65,6 +67,25 @@ def test_greedy_continuation_is_the_argmax():
 
 def _lib():
     return ops.ext().lib
+
+
+@torch.no_grad()
+def test_epilogue_decoder_matches_separate_kernels():
+    """The epilogue-fused step computes the separate kernels' values; only the RMSNorms' sums of squares run in
+    another order (an fp16 ulp of the normalized row), so logits agree closely and the launch count drops by 3 per
+    layer."""
+    decode.enable_decode_options()
+    prompt = torch.arange(12) * 53 % TINY["vocab_size"]
+    seq = (torch.arange(8) * 97 % TINY["vocab_size"]).tolist()
+    plain = decode.Int4Decoder(decode.build(TINY, seed=7), max_len=32)
+    fused = decode.Int4Decoder(decode.build(TINY, seed=7), max_len=32, fuse=("epilogue",))
+    assert plain.launches_per_step() - fused.launches_per_step() == 3 * TINY["num_hidden_layers"]
+    plain.prefill(prompt)
+    fused.prefill(prompt)
+    a, b = plain.forced(seq), fused.forced(seq)
+    assert (a - b).abs().max() / a.pow(2).mean().sqrt() < 5e-3
+    assert torch.equal(a.argmax(-1), b.argmax(-1))
+    assert _lib().lb_device_error() == 0
 
 
 def _stream():
@@ -193,6 +214,104 @@ def test_swiglu_gemv_is_silu_mul_then_gemv(nk):
     want = ops.gemv(a, wq, 6)
     torch.cuda.synchronize()
     assert torch.equal(y, want)
+
+
+def _ulp_close(a, b, ulps=1):
+    """fp16 tensors equal up to `ulps` units in the last place of the larger magnitude (normalizations whose sums of
+    squares run in another order)."""
+    a, b = a.float(), b.float()
+    ulp = torch.maximum(a.abs(), b.abs()).clamp_min(2.0 ** -14)
+    ulp = torch.exp2(torch.floor(torch.log2(ulp)) - 10)
+    return bool(((a - b).abs() <= ulps * ulp).all())
+
+
+# (N, K, forced row tiles): 3B gate|up, a 0.5B-like gate|up, a K long enough for the cluster split-K path, two
+# 16-row tiles per CTA
+@pytest.mark.parametrize("nkr", [(22016, 2048, 0), (9728, 896, 0), (1024, 18944, 0), (4096, 2048, 2)])
+def test_gemv_swiglu_epilogue_is_gemv_then_silu_mul(nkr):
+    """lb_decode_gemv_swiglu on rows interleaving gate and up: bit-identical to the plain GEMV (lb_w4_gemv version
+    6) followed by lb_decode_silu_mul on the de-interleaved [gate | up] row."""
+    n, k, rt = nkr
+    wq = _w4(n, k, 3 * n + k)
+    g = torch.Generator(device="cuda").manual_seed(k)
+    x = torch.randn(1, k, device="cuda", generator=g).half()
+    e = ops.ext()
+    prev = e.set_option("gemv_rowtiles", rt)
+    try:
+        y = ops.gemv(x, wq, 6)
+        a = torch.full((n // 2,), float("nan"), device="cuda").half()
+        rc = _lib().lb_decode_gemv_swiglu(x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(), a.data_ptr(),
+                                          n, k, 128, _stream())
+        assert rc == 0, _lib().lb_last_error()
+    finally:
+        e.set_option("gemv_rowtiles", prev)
+    gu = torch.cat([y[0, 0::2], y[0, 1::2]]).contiguous()
+    want = torch.empty(n // 2, device="cuda").half()
+    assert _lib().lb_decode_silu_mul(gu.data_ptr(), want.data_ptr(), n // 2, _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(a, want)
+
+
+# (N, K): 3B o and down, 7B down on one GPU (K split over a cluster), 0.5B o
+@pytest.mark.parametrize("nk", [(2048, 2048), (2048, 11008), (3584, 18944), (896, 896)])
+def test_gemv_residual_norm_epilogue(nk):
+    """lb_decode_gemv_residual_norm: y has the plain GEMV's bits, the residual stream gets x + y (one fp16
+    rounding), h matches lb_decode_rmsnorm to an fp16 ulp, and the counter is left zero, so a second call in a row
+    (another residual row) is right too."""
+    n, k = nk
+    wq = _w4(n, k, n + 5 * k)
+    g = torch.Generator(device="cuda").manual_seed(n)
+    ln = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).half()
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for call in range(2):
+        x = torch.randn(1, k, device="cuda", generator=g).half()
+        res = (4 * torch.randn(n, device="cuda", generator=g)).half()
+        res0 = res.clone()
+        y = torch.empty(1, n, device="cuda").half()
+        h = torch.full((n,), float("nan"), device="cuda").half()
+        rc = _lib().lb_decode_gemv_residual_norm(x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(),
+                                                 y.data_ptr(), n, k, 128, res.data_ptr(), ln.data_ptr(), h.data_ptr(),
+                                                 1e-6, counter.data_ptr(), _stream())
+        assert rc == 0, _lib().lb_last_error()
+        want_y = ops.gemv(x, wq, 6)
+        xs, want_h = res0.clone(), torch.empty(n, device="cuda").half()
+        assert _lib().lb_decode_rmsnorm(xs.data_ptr(), want_y.data_ptr(), ln.data_ptr(), want_h.data_ptr(), n, 1e-6,
+                                        _stream()) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y, want_y), call
+        assert torch.equal(res, xs), call
+        assert _ulp_close(h, want_h), call
+        assert counter.item() == 0
+
+
+def test_tp_allreduce_norm_simulated_peer():
+    """lb_tp_allreduce_norm at world 2 with the peer simulated on this GPU: the residual stream gets x + the
+    rank-ordered sum, h matches lb_decode_rmsnorm on it to an fp16 ulp, and the input is left as it was."""
+    lib, cap, n = _lib(), 4096, 3584
+    mine = torch.zeros(128 + 2 * cap, device="cuda").half()
+    peer = torch.zeros(128 + 2 * cap, device="cuda").half()
+    epoch = torch.ones(1, device="cuda", dtype=torch.int32)     # epoch 1 -> 2: slot 0
+    g = torch.Generator(device="cuda").manual_seed(3)
+    t = torch.randn(n, device="cuda", generator=g).half()
+    other = torch.randn(n, device="cuda", generator=g).half()
+    peer[128:128 + n] = other
+    mine.view(torch.int32)[1] = 2
+    res = (4 * torch.randn(n, device="cuda", generator=g)).half()
+    res0, t0 = res.clone(), t.clone()
+    ln = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).half()
+    h = torch.full((n,), float("nan"), device="cuda").half()
+    bufs = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    assert lib.lb_tp_allreduce_norm(t.data_ptr(), n, cap, bufs.data_ptr(), epoch.data_ptr(), 0, 2, res.data_ptr(),
+                                    ln.data_ptr(), h.data_ptr(), 1e-6, _stream()) == 0
+    total = (t0.float() + other.float()).half()
+    xs, want_h = res0.clone(), torch.empty(n, device="cuda").half()
+    assert lib.lb_decode_rmsnorm(xs.data_ptr(), total.data_ptr(), ln.data_ptr(), want_h.data_ptr(), n, 1e-6,
+                                 _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(t, t0) and epoch.item() == 2
+    assert torch.equal(res, xs)
+    assert _ulp_close(h, want_h)
+    assert lib.lb_device_error() == 0
 
 
 def test_decode_gemv_fusable_rule():

@@ -79,6 +79,8 @@ def test_sharded_quantization_is_bit_identical(world):
             assert np.array_equal(pk, full["o"][0][:, q0 * 32:q1 * 32])
         pk, _ = quant.quantize_w4(sh["gu"].numpy(), 128)
         assert np.array_equal(pk, np.concatenate([full["gate"][0][i0:i1], full["up"][0][i0:i1]]))
+        pk, _ = quant.quantize_w4(tp.shard_layer(w, p, interleave=True)["gu"].numpy(), 128)
+        assert np.array_equal(pk[0::2], full["gate"][0][i0:i1]) and np.array_equal(pk[1::2], full["up"][0][i0:i1])
 
 
 def _free_port():

@@ -19,7 +19,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, results):
+def _rank(rank, world, port, results, fuse=()):
     from datetime import timedelta
     import torch.distributed as dist
     from lowbit import decode
@@ -33,7 +33,7 @@ def _rank(rank, world, port, results):
         prompt = torch.randint(0, TINY["vocab_size"], (20,), generator=gen)
         seq = torch.randint(0, TINY["vocab_size"], (10,), generator=gen).tolist()
         dec = decode.Int4Decoder(decode.build(TINY, seed=3, device=dev), 48, world=world, rank=rank,
-                                 pg=dist.group.WORLD)
+                                 pg=dist.group.WORLD, fuse=fuse)
         dec.prefill(prompt)
         got = dec.forced(seq)
         toks = []
@@ -60,10 +60,12 @@ def _rank(rank, world, port, results):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_decoder_matches_single_gpu():
+@pytest.mark.parametrize("fuse", [(), ("epilogue",)])
+def test_tp2_decoder_matches_single_gpu(fuse):
+    """fuse=("epilogue",): the residual add + RMSNorm run inside the one-shot allreduce"""
     world = 2
     results = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_rank, args=(world, _free_port(), results), nprocs=world, start_method="spawn")
+    mp.start_processes(_rank, args=(world, _free_port(), results, fuse), nprocs=world, start_method="spawn")
     for r in range(world):
         assert results[f"err{r}"] < 2e-2, results[f"err{r}"]
         toks, ref_toks = results[f"toks{r}"]
