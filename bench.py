@@ -683,9 +683,18 @@ def profile_sweep(passes=2):
     print(f"profile sweep: {passes} passes x {len(projs)} calls", file=sys.stderr)
 
 
+# measured defaults (B200): config 3 runs fastest with the separate kernels; config 4 with the o and down GEMVs
+# fused with their allreduce, residual add and RMSNorm (TP2 488 tok/s against 474 for GEMV then allreduce + norm)
+DEFAULT_FUSE = {3: "", 4: "epilogue,gemv_allreduce"}
+
+
 def fuse_arg(args):
-    """--fuse: comma-separated kernel fusions of the decode step (Int4Decoder's `fuse`)."""
-    return tuple(f for f in getattr(args, "fuse", "").split(",") if f)
+    """--fuse: comma-separated kernel fusions of the decode step (Int4Decoder's `fuse`); the config's measured
+    default when not given."""
+    f = getattr(args, "fuse", None)
+    if f is None:
+        f = DEFAULT_FUSE.get(getattr(args, "config", 3), "")
+    return tuple(x for x in f.split(",") if x)
 
 
 def profile_decode(fuse=(), steps=3, prompt_len=8):
@@ -716,9 +725,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",
                     help="config 4: row-parallel sums by the library's one-shot kernel or by NCCL")
-    ap.add_argument("--fuse", default="",
+    ap.add_argument("--fuse", default=None,
                     help="configs 3, 4: decode-step fusions, comma-separated: epilogue (norms and SwiGLU in the "
-                         "GEMV / allreduce epilogues) or any of qkv, gu, down (GEMV prologues)")
+                         "GEMV / allreduce epilogues), gemv_allreduce (config 4: o and down GEMVs fused with their "
+                         "allreduce) or any of qkv, gu, down (GEMV prologues); --fuse= for none")
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",

@@ -174,6 +174,22 @@ LB_API int lb_tp_allreduce_norm(const void* in, int64_t n, int64_t cap, void* co
                          int world, void* x_res, const void* norm_w, void* h_out, float eps, lb_stream_t stream);
 
 /*
+ * Row-parallel decode GEMV fused with the allreduce, residual add and RMSNorm of tensor-parallel decode (one kernel
+ * per call on every rank): y_rank = W_rank x over this rank's K shard; x_res += sum over ranks of y_r (fp16
+ * partials summed in rank order in fp32, one rounding -- the bits of lb_w4_gemv version 6 followed by
+ * lb_tp_allreduce_norm); h_out = norm_w * fp16(x_res * rsqrt(mean(x_res^2) + eps)); y (may be null) receives the
+ * sum. Each finished 16-row tile is stored over NVLink into every rank's buffer as it completes, as 8-byte words
+ * (epoch << 32 | two fp16 outputs) that validate themselves; the last CTA polls only local memory until every
+ * rank's words carry the epoch (at most ~1 s, then lb_device_error() = 2). bufs[r]: rank r's peer-mapped buffer
+ * of 256 bytes of header + 2 * world * cap * 4 bytes (zeroed before first use, not shared with lb_tp_allreduce),
+ * epoch: this rank's device counter (equal on every rank), counter: a device int, zero before the first call.
+ */
+LB_API int lb_tp_gemv_allreduce_norm(const void* x, const void* w, const void* scales, void* y, int64_t n, int64_t k,
+                              int64_t group, int64_t cap, void* const* bufs, uint32_t* epoch, int rank, int world,
+                              void* x_res, const void* norm_w, void* h_out, float eps, int* counter,
+                              lb_stream_t stream);
+
+/*
  * Decode GEMVs with the following step in their epilogue: M = 1, the kernel, K split and row tiling of lb_w4_gemv
  * version 6 at M = 1 (so y has its bits), K a multiple of 128:
  * lb_decode_gemv_swiglu:        W's rows interleave gate and up (row 2i = gate_i, row 2i + 1 = up_i, N % 16 == 0);

@@ -539,6 +539,42 @@ int lb_decode_gemv_residual_norm(const void* x, const void* w, const void* scale
   return epi_gemv(p, n, k, group, stream);
 }
 
+int lb_tp_gemv_allreduce_norm(const void* x, const void* w, const void* scales, void* y, int64_t n, int64_t k,
+                              int64_t group, int64_t cap, void* const* bufs, uint32_t* epoch, int rank, int world,
+                              void* x_res, const void* norm_w, void* h_out, float eps, int* counter,
+                              lb_stream_t stream) {
+  if (!bufs || !epoch || !x_res || !norm_w || !h_out || !counter) return fail(LB_ERR_ARGUMENT, "null pointer argument");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(LB_ERR_ARGUMENT, "rank %d of world %d (at most 64 ranks)", rank, world);
+  if (n % 8 || cap % 8 || cap < n || cap > (1 << 26))
+    return fail(LB_ERR_ARGUMENT, "N = %lld must be a multiple of 8 within the slot capacity %lld (a multiple of 8)",
+                (long long)n, (long long)cap);
+  if (((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_res) | reinterpret_cast<uintptr_t>(norm_w) |
+        reinterpret_cast<uintptr_t>(h_out)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "y, x_res, norm_w and h_out must be 16-byte aligned");
+  lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), 1, (int)n, (int)k, (int)group,
+                   g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
+                   (int)(group / 128)};
+  p.epi = 3;
+  p.epi_counter = counter;
+  p.epi_x = static_cast<__half*>(x_res);
+  p.epi_w = static_cast<const __half*>(norm_w);
+  p.epi_h = static_cast<__half*>(h_out);
+  p.epi_eps = eps;
+  p.ar_bufs = reinterpret_cast<uint8_t* const*>(bufs);
+  p.ar_epoch = epoch;
+  p.ar_rank = rank;
+  p.ar_world = world;
+  p.ar_cap = (int)cap;
+  int rc = check_common(x, w, scales, y ? y : x_res, 1, n, k, group);
+  if (rc) return rc;
+  if (k % 128 || group % 128)
+    return fail(LB_ERR_ARGUMENT, "the fused decode GEMV needs K and the group size to be multiples of 128");
+  const lb::OneshotConfig c = oneshot_config(1, (int)n, (int)k);
+  if (c.warps == 0) return fail(LB_ERR_UNSUPPORTED, "K=%lld is too long for the one-shot GEMV", (long long)k);
+  return launched(lb::launch_gemv_oneshot(p, c, reinterpret_cast<cudaStream_t>(stream)), "tp_gemv_allreduce_norm");
+}
+
 int lb_decode_silu_mul(const void* gu, void* a, int64_t I, lb_stream_t stream) {
   if (!gu || !a) return fail(LB_ERR_ARGUMENT, "null pointer argument");
   if (I <= 0 || I > (1 << 28)) return fail(LB_ERR_ARGUMENT, "bad size %lld", (long long)I);

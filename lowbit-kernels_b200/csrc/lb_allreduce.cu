@@ -24,17 +24,6 @@ __device__ int g_ar_status;
 namespace {
 
 constexpr int kArThreads = 512;
-constexpr long long kArWaitCycles = 2000000000LL;   // ~1 s at B200 clocks
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __device__ __forceinline__ uint4 ld_u4_volatile(const void* p) {
   uint4 v;
@@ -60,7 +49,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
   pdl_wait();   // `in` comes from the previous kernel in the stream
   const uint32_t e = *epoch_p + 1;
   const int slot = e & 1, n8 = n / 8;
-  const size_t flag_bytes = 256, slot_bytes = (size_t)cap * 2;
+  const size_t flag_bytes = kPeerFlagBytes, slot_bytes = (size_t)cap * 2;
   uint8_t* mine = bufs[rank];
   uint4* my_slot = reinterpret_cast<uint4*>(mine + flag_bytes + slot * slot_bytes);
   for (int v = threadIdx.x; v < n8; v += blockDim.x) {   // L2-cached load: `in` was just written by another kernel
@@ -77,17 +66,9 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
     for (int r = 0; r < world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(bufs[r]) + rank, e);
   }
   // wait for every rank's epoch (thread r polls rank r's flag in this rank's buffer)
-  if (threadIdx.x < world) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine) + threadIdx.x;
-    const long long t0 = clock64();
-    while ((int)(ld_acquire_sys(f) - e) < 0) {
-      if (clock64() - t0 > kArWaitCycles) {
-        atomicExch(&g_ar_status, kErrPeerTimeout);
-        timed_out = 1;
-        break;
-      }
-    }
-  }
+  if (threadIdx.x < world &&
+      !wait_peer_epoch(reinterpret_cast<const uint32_t*>(mine) + threadIdx.x, e, &g_ar_status))
+    timed_out = 1;
   __syncthreads();
   float ss_part = 0.f;
   for (int v = threadIdx.x; v < n8; v += blockDim.x) {

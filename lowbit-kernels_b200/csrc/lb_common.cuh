@@ -117,6 +117,35 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrBarrierTimeout = 1;
 constexpr int kErrPeerTimeout = 2;    // a peer rank did not publish its epoch in time (allreduce)
 
+// ------------------------------------------------------------------------------------- peer-memory epochs
+// Row-parallel sums over NVLink peer memory: every rank owns a peer-mapped buffer that starts with
+// kPeerFlagBytes of per-rank epoch flags (flag r = the last epoch rank r has published into this buffer).
+constexpr int kPeerFlagBytes = 256;
+constexpr long long kPeerWaitCycles = 2000000000LL;   // ~1 s at B200 clocks, then kErrPeerTimeout
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Poll flag f until it reaches epoch e (wrap-around safe) for at most kPeerWaitCycles; false on timeout, after
+// recording kErrPeerTimeout in *status
+__device__ __forceinline__ bool wait_peer_epoch(const uint32_t* f, uint32_t e, int* status) {
+  const long long t0 = clock64();
+  while ((int)(ld_acquire_sys(f) - e) < 0) {
+    if (clock64() - t0 > kPeerWaitCycles) {
+      atomicExch(status, kErrPeerTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -292,6 +292,16 @@ __device__ __forceinline__ float cta_sum_f32(float v, float* red) {
   return warp_sum(t);
 }
 
+__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // fetch-and-add with acquire-release semantics at GPU scope: publishes what this thread (and, after a bar.sync,
 // its CTA) wrote before it and makes visible what the earlier adders published
 __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(int* p, unsigned v) {
@@ -564,14 +574,16 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     }
     return;
   }
-  for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, tile_sum(e));
-  if constexpr (EPI == 2) {
-    // the last row tile to finish adds the whole output row into the residual stream and normalizes it (the
-    // counter counts the tiles' finishing CTAs -- rank 0 of each cluster -- and is left zero for the next call).
+  if constexpr (EPI != 3) {
+    for (int e = threadIdx.x; e < kTile; e += blockDim.x) store(e, tile_sum(e));
+  }
+  if constexpr (EPI == 2 || EPI == 3) {
+    // the last row tile to finish (the counter counts the tiles' finishing CTAs -- rank 0 of each cluster -- and
+    // is left zero for the next call) adds the whole output row into the residual stream and normalizes it.
     // Every such CTA first loads its pieces of the residual row and the norm weights (neither is written by this
-    // kernel before the count completes), so the last one starts its reduction with only y still to read.
+    // kernel before the count completes), so the last one starts with only y still to read.
     constexpr int kPre = 4;   // pieces held per thread: N <= 8 * kPre * blockDim covers N <= 8192 at 256 threads
-    __shared__ int last;
+    __shared__ int last, timed_out;
     __shared__ float epi_red[32];
     const int n8 = N / 8;
     uint4 xpre[kPre], wpre[kPre];
@@ -583,13 +595,80 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
         wpre[j] = ldg_stream(reinterpret_cast<const uint4*>(p.epi_w) + v);
       }
     }
-    __syncthreads();   // this CTA's y stores precede thread 0's release below (bar.sync, then a cumulative release)
-    if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(p.epi_counter, 1) == gridDim.x - 1;
+    uint32_t ep = 0;
+    if constexpr (EPI == 3) {
+      // this tile's fp16 partial, pushed over NVLink into region (ep & 1, rank) of every rank's buffer as
+      // self-validating 8-byte words (epoch << 32 | two fp16 outputs): a reader polls each word until it carries
+      // the epoch, so the pushes need no fence and no flag
+      __shared__ __align__(16) __half tile_h[16 * RT];
+      __shared__ uint32_t ep_s;
+      if (threadIdx.x == 0) ep_s = *reinterpret_cast<volatile uint32_t*>(p.ar_epoch) + 1;
+      for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
+        const int rm = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+        const int r = rm / MT, mt = rm - r * MT;
+        if (mt == 0 && (ln & 3) == 0 && (i & 1) == 0)   // activation row 0
+          tile_h[16 * r + (ln >> 2) + (i >= 2 ? 8 : 0)] = __float2half_rn(tile_sum(e));
+      }
+      __syncthreads();
+      ep = ep_s;
+      const int world = p.ar_world;
+      for (int j = threadIdx.x; j < 8 * RT * world; j += blockDim.x) {
+        const int dst = j / (8 * RT), wi = j - dst * (8 * RT);
+        const int row = n0 + 2 * wi;
+        if (row + 2 <= N) {
+          uint64_t* region = reinterpret_cast<uint64_t*>(p.ar_bufs[dst] + kPeerFlagBytes) +
+                             (size_t)((ep & 1) * world + p.ar_rank) * (p.ar_cap / 2);
+          const uint32_t data = reinterpret_cast<const uint32_t*>(tile_h)[wi];
+          st_volatile_u64(region + row / 2, ((uint64_t)ep << 32) | data);
+        }
+      }
+    }
+    __syncthreads();   // this CTA's stores precede thread 0's release (bar.sync, then a cumulative release)
+    if (threadIdx.x == 0) {
+      last = atom_add_acq_rel_gpu(p.epi_counter, 1) == gridDim.x - 1;
+      timed_out = 0;
+    }
     __syncthreads();
     if (!last) return;
+    // piece v of the finished output row: y as stored above, or the rank-ordered fp32 sum of the ranks' words
+    // (each polled, for at most ~1 s in all, until it carries this epoch)
+    const long long t_wait = clock64();
+    auto y_piece = [&](int v) -> uint4 {
+      if constexpr (EPI == 2) {
+        return ldg_cg_u4(p.y + 8 * (size_t)v);
+      } else {
+        const uint64_t* base = reinterpret_cast<const uint64_t*>(p.ar_bufs[p.ar_rank] + kPeerFlagBytes) +
+                               (size_t)(ep & 1) * p.ar_world * (p.ar_cap / 2) + 4 * (size_t)v;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < p.ar_world; ++r) {
+          const uint64_t* src = base + (size_t)r * (p.ar_cap / 2);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint64_t wv = ld_volatile_u64(src + k);
+            while ((uint32_t)(wv >> 32) != ep) {
+              if (clock64() - t_wait > kPeerWaitCycles) {
+                atomicExch(&g_device_status, kErrPeerTimeout);
+                timed_out = 1;
+                break;
+              }
+              wv = ld_volatile_u64(src + k);
+            }
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv));
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) oh[k] = __floats2half2_rn(acc[2 * k], acc[2 * k + 1]);
+        if (p.y) reinterpret_cast<uint4*>(p.y)[v] = o;
+        return o;
+      }
+    };
     float ss = 0.f;
     auto add_piece = [&](int v, uint4& xv) {
-      const uint4 yv = ldg_cg_u4(p.y + 8 * (size_t)v);
+      const uint4 yv = y_piece(v);
       __half2* xh = reinterpret_cast<__half2*>(&xv);
       const __half2* yh = reinterpret_cast<const __half2*>(&yv);
 #pragma unroll
@@ -631,7 +710,13 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
       const uint4 xv = reinterpret_cast<const uint4*>(p.epi_x)[v];
       norm_piece(v, xv, ldg_stream(reinterpret_cast<const uint4*>(p.epi_w) + v), inv);
     }
-    if (threadIdx.x == 0) *p.epi_counter = 0;
+    __syncthreads();   // timed_out is final
+    if (threadIdx.x == 0) {
+      *p.epi_counter = 0;
+      if constexpr (EPI == 3) {
+        if (!timed_out) *p.ar_epoch = ep;
+      }
+    }
   }
 }
 
@@ -684,7 +769,8 @@ cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cud
     if (p.epi == EPI_ && c.rt == RT_ && c.cpw == CPW_) return launch_oneshot_t<1, RT_, CPW_, 0, EPI_>(p, c, st);
     LB_ONESHOT_EPI(1, 1, 2) LB_ONESHOT_EPI(1, 1, 4) LB_ONESHOT_EPI(1, 1, 8) LB_ONESHOT_EPI(1, 2, 2)
     LB_ONESHOT_EPI(1, 2, 4) LB_ONESHOT_EPI(2, 1, 2) LB_ONESHOT_EPI(2, 1, 4) LB_ONESHOT_EPI(2, 1, 8)
-    LB_ONESHOT_EPI(2, 2, 2) LB_ONESHOT_EPI(2, 2, 4)
+    LB_ONESHOT_EPI(2, 2, 2) LB_ONESHOT_EPI(2, 2, 4) LB_ONESHOT_EPI(3, 1, 2) LB_ONESHOT_EPI(3, 1, 4)
+    LB_ONESHOT_EPI(3, 1, 8) LB_ONESHOT_EPI(3, 2, 2) LB_ONESHOT_EPI(3, 2, 4)
 #undef LB_ONESHOT_EPI
     return cudaErrorInvalidConfiguration;
   }

@@ -34,12 +34,20 @@ struct GemvParams {
   // (W rows 2i, 2i + 1 = gate_i, up_i): y[i] = fp16(fp16(silu(fp16(gate_i))) * fp16(up_i)), N / 2 outputs; 2 y is
   // stored, then the last CTA to finish (epi_counter, zero between calls) adds y into the residual stream epi_x
   // and writes epi_h = epi_w * fp16(x * rsqrt(mean(x^2) + eps)) for the next projection
+  // 3 (row-parallel, tensor parallelism): each finished tile's fp16 partial is stored into region (e & 1, ar_rank)
+  // of every rank's peer-mapped buffer (kPeerFlagBytes of header, then 2 x ar_world regions of ar_cap / 2 words
+  // e << 32 | two fp16, region (parity, source rank)), e = *ar_epoch + 1; the last CTA polls its own buffer's
+  // words until each carries e, sums the ranks in rank order (y, if not null, receives the sum), then continues
+  // as 2
   int epi = 0;
   int* epi_counter = nullptr;
   __half* epi_x = nullptr;
   const __half* epi_w = nullptr;
   __half* epi_h = nullptr;
   float epi_eps = 0.f;
+  uint8_t* const* ar_bufs = nullptr;
+  uint32_t* ar_epoch = nullptr;
+  int ar_rank = 0, ar_world = 1, ar_cap = 0;
 };
 
 struct GemvConfig {

@@ -43,6 +43,8 @@ SIGNATURES = {
     "lb_tp_allreduce": ([_P, _P, _I64, _I64, _P, _P, _I, _I, _P], _I),
     "lb_tp_allreduce_norm": ([_P, _I64, _I64, _P, _P, _I, _I, _P, _P, _P, ctypes.c_float, _P], _I),
     "lb_decode_gemv_swiglu": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], _I),
+    "lb_tp_gemv_allreduce_norm": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I, _I, _P, _P, _P, ctypes.c_float,
+                                   _P, _P], _I),
     "lb_decode_gemv_residual_norm": ([_P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_float, _P, _P], _I),
     "lb_decode_norm_gemv": ([_P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I64, _I64, _I64, _P], _I),
     "lb_decode_swiglu_gemv": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], _I),

@@ -147,8 +147,10 @@ class Int4Decoder:
     `fuse` picks kernel fusions: "norm_epilogue" ends the o and down GEMVs with the residual add + next RMSNorm
     (the last CTA of the GEMV, or the one-shot allreduce under tensor parallelism); "swiglu_epilogue" ends the
     gate|up GEMV with SiLU*up (its rows interleaved); "epilogue" is both, so a layer is q|k|v GEMV, attention, o,
-    gate|up, down. "qkv", "gu", "down" instead fold the preceding norm or SwiGLU into the GEMV's prologue where
-    one CTA holds the row."""
+    gate|up, down; under tensor parallelism with the one-shot allreduce, "gemv_allreduce" also fuses the o and down
+    GEMVs with their allreduce (each finished tile pushed over NVLink into every rank's buffer, the last CTA
+    summing and normalizing: one kernel instead of two). "qkv", "gu", "down" instead fold the preceding norm or
+    SwiGLU into the GEMV's prologue where one CTA holds the row."""
 
     def __init__(self, model, max_len, group=128, world=1, rank=0, pg=None, fuse=(), allreduce="oneshot"):
         e = ops.ext()
@@ -160,7 +162,8 @@ class Int4Decoder:
         self.eps = float(cfg.rms_norm_eps)
         self.max_len = max_len
         self.world, self.rank, self.pg = world, rank, pg
-        self.epi_norm = "epilogue" in fuse or "norm_epilogue" in fuse
+        self.gemv_ar = world > 1 and allreduce == "oneshot" and "gemv_allreduce" in fuse
+        self.epi_norm = "epilogue" in fuse or "norm_epilogue" in fuse or self.gemv_ar
         self.epi_swiglu = "epilogue" in fuse or "swiglu_epilogue" in fuse
         self.epilogue = self.epi_norm or self.epi_swiglu
         theta = float(cfg.rope_parameters["rope_theta"])
@@ -267,6 +270,9 @@ class Int4Decoder:
                 self.x.data_ptr(), ln.data_ptr(), self.h.data_ptr(), self.eps, self.counters.data_ptr() + 4 * slot,
                 st))
             return
+        if self.gemv_ar:
+            self.allreduce.gemv_residual_norm(x, wq, self.x, ln, self.h, self.eps, self.counters[slot:slot + 1])
+            return
         y = ops.gemv(x, wq, 6)
         if self.epi_norm and isinstance(self.allreduce, tp.OneShotAllReduce):
             self.allreduce.residual_norm(y, self.x, ln, self.h, self.eps)
@@ -368,7 +374,7 @@ class Int4Decoder:
         oneshot = 2 * isinstance(self.allreduce, tp.OneShotAllReduce)   # the o and down allreduces of a layer
         if self.epilogue:   # q|k|v, attention (2), o, gate|up, down + the unfused norms and SiLU*up
             norms = 0 if self.epi_norm and (self.world == 1 or oneshot) else 2
-            ar = oneshot if self.world > 1 else 0
+            ar = oneshot if self.world > 1 and not self.gemv_ar else 0
             per = 6 + ar + norms + (not self.epi_swiglu)
             return 2 + per * len(self.layers)
         per = sum(6 + oneshot + (not ly["fuse_qkv"]) + (not ly["fuse_gu"]) + (not ly["fuse_down"])

@@ -72,7 +72,9 @@ def shard_layer(w, p, interleave=False):
 class OneShotAllReduce:
     """In-place sum allreduce of small fp16 tensors for tensor-parallel decode: the library's one-shot kernel
     (lb_tp_allreduce: one launch per call on each rank, peer loads over NVLink, bounded waits) on peer-mapped
-    buffers that torch's symmetric memory allocates and exchanges (plumbing only)."""
+    buffers that torch's symmetric memory allocates and exchanges (plumbing only). The same allocation holds a
+    second region for the row-parallel GEMV fused with the allreduce (lb_tp_gemv_allreduce_norm), which pushes
+    each finished tile into every rank's region and has its own epoch."""
 
     FLAG_BYTES = 256
 
@@ -90,13 +92,17 @@ class OneShotAllReduce:
             symm.enable_symm_mem_for_group(group.group_name)
         except Exception:   # noqa: BLE001 - newer torch enables groups on first use
             pass
-        self.buf = symm.empty(self.FLAG_BYTES // 2 + 2 * self.cap, dtype=torch.half, device=device)
+        pull = self.FLAG_BYTES // 2 + 2 * self.cap                  # halves: flags + 2 slots
+        push = self.FLAG_BYTES // 2 + 4 * self.world * self.cap      # header + 2 x world regions of cap / 2 words
+        self.buf = symm.empty(pull + push, dtype=torch.half, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
         handle = symm.rendezvous(self.buf, group)
         off = self.buf.data_ptr() - handle.buffer_ptrs[self.rank]
         self.ptrs = torch.tensor([p + off for p in handle.buffer_ptrs], dtype=torch.int64, device=device)
+        self.push_ptrs = self.ptrs + 2 * pull
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.push_epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.handle = handle
         dist.barrier(group)
 
@@ -108,6 +114,17 @@ class OneShotAllReduce:
         if rc:
             raise RuntimeError(self.lib.lb_last_error().decode())
         return t
+
+    def gemv_residual_norm(self, x, wq, x_res, norm_w, h, eps, counter):
+        """One kernel: this rank's row-parallel GEMV partial W x, summed over the ranks, added into x_res; h =
+        RMSNorm(x_res) * norm_w (lb_tp_gemv_allreduce_norm). counter: a zeroed device int32 of this call site."""
+        import torch
+        rc = self.lib.lb_tp_gemv_allreduce_norm(
+            x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(), None, wq.n, wq.k, wq.group, self.cap,
+            self.push_ptrs.data_ptr(), self.push_epoch.data_ptr(), self.rank, self.world, x_res.data_ptr(),
+            norm_w.data_ptr(), h.data_ptr(), eps, counter.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        if rc:
+            raise RuntimeError(self.lib.lb_last_error().decode())
 
     def residual_norm(self, t, x_res, norm_w, h, eps):
         """x_res += the sum of every rank's t; h = RMSNorm(x_res) * norm_w (lb_tp_allreduce_norm, one launch);

@@ -314,6 +314,108 @@ def test_tp_allreduce_norm_simulated_peer():
     assert lib.lb_device_error() == 0
 
 
+def _fused_ar_call(lib, x, wq, y, cap, bufs, epoch, rank, world, res, ln, h, counter):
+    return lib.lb_tp_gemv_allreduce_norm(x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(),
+                                         None if y is None else y.data_ptr(), wq.n, wq.k, 128, cap, bufs.data_ptr(),
+                                         epoch.data_ptr(), rank, world, res.data_ptr(), ln.data_ptr(), h.data_ptr(),
+                                         1e-6, counter.data_ptr(), _stream())
+
+
+def _ll_words(half_vec, epoch):
+    """fp16 [n] -> the fused allreduce's n / 2 words: epoch << 32 | two fp16 outputs (little-endian pair)."""
+    bits = half_vec.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    return bits | (epoch << 32)
+
+
+# (N, K): 7B o and down at tensor-parallel degree 2 (down splits K over a cluster at degree 1: 18944), 3B down at 2
+@pytest.mark.parametrize("nk", [(3584, 1792), (3584, 9472), (2048, 5504), (3584, 18944)])
+def test_tp_gemv_allreduce_norm_simulated_peer(nk):
+    """lb_tp_gemv_allreduce_norm at world 2 with the peer simulated on this GPU (its partial written beforehand as
+    epoch-tagged words): this rank's tiles land in region (0, rank 0) of both buffers tagged with epoch 2, the sum
+    is rank 0's GEMV bits plus the peer's partial (fp32, one rounding), the residual and h match lb_decode_rmsnorm,
+    the epoch advances."""
+    n, k = nk
+    lib, cap = _lib(), n
+    wq = _w4(n, k, 11 * n + k)
+    g = torch.Generator(device="cuda").manual_seed(k)
+    x = torch.randn(1, k, device="cuda", generator=g).half()
+    other = torch.randn(n, device="cuda", generator=g).half()
+    res = (4 * torch.randn(n, device="cuda", generator=g)).half()
+    ln = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).half()
+    res0 = res.clone()
+    words = 32 + 4 * cap // 2       # int64 words: 256 bytes of header, then 2 parities x 2 ranks x cap / 2
+    mine = torch.zeros(words, device="cuda", dtype=torch.int64)
+    peer = torch.zeros(words, device="cuda", dtype=torch.int64)
+    region = lambda buf, par, src: buf[32 + (2 * par + src) * (cap // 2):32 + (2 * par + src) * (cap // 2) + n // 2]
+    epoch = torch.ones(1, device="cuda", dtype=torch.int32)      # epoch 1 -> 2: parity 0
+    region(mine, 0, 1).copy_(_ll_words(other, 2))
+    bufs = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    counter = torch.zeros(1, device="cuda", dtype=torch.int32)
+    y = torch.full((n,), float("nan"), device="cuda").half()
+    h = torch.full((n,), float("nan"), device="cuda").half()
+    assert _fused_ar_call(lib, x, wq, y, cap, bufs, epoch, 0, 2, res, ln, h, counter) == 0, lib.lb_last_error()
+    part = ops.gemv(x, wq, 6)[0]
+    total = (part.float() + other.float()).half()
+    xs, want_h = res0.clone(), torch.empty(n, device="cuda").half()
+    assert lib.lb_decode_rmsnorm(xs.data_ptr(), total.data_ptr(), ln.data_ptr(), want_h.data_ptr(), n, 1e-6,
+                                 _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(region(mine, 0, 0), _ll_words(part, 2)) and torch.equal(region(peer, 0, 0), _ll_words(part, 2))
+    assert torch.equal(y, total)
+    assert torch.equal(res, xs)
+    assert _ulp_close(h, want_h)
+    assert epoch.item() == 2 and counter.item() == 0
+    assert lib.lb_device_error() == 0
+
+
+def test_tp_gemv_allreduce_norm_world_one_is_the_residual_norm_gemv():
+    """At world 1 the fused kernel's residual and h have the bits of lb_decode_gemv_residual_norm."""
+    n, k = 2048, 2048
+    lib = _lib()
+    wq = _w4(n, k, 5)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(1, k, device="cuda", generator=g).half()
+    res = (4 * torch.randn(n, device="cuda", generator=g)).half()
+    ln = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).half()
+    res2 = res.clone()
+    buf = torch.zeros(32 + n, device="cuda", dtype=torch.int64)     # header + 2 parities x 1 rank x n / 2 words
+    bufs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device="cuda")
+    epoch = torch.zeros(1, device="cuda", dtype=torch.int32)
+    c1, c2 = torch.zeros(1, device="cuda", dtype=torch.int32), torch.zeros(1, device="cuda", dtype=torch.int32)
+    h1, h2 = torch.empty(n, device="cuda").half(), torch.empty(n, device="cuda").half()
+    assert _fused_ar_call(lib, x, wq, None, n, bufs, epoch, 0, 1, res, ln, h1, c1) == 0, lib.lb_last_error()
+    y = torch.empty(1, n, device="cuda").half()
+    assert lib.lb_decode_gemv_residual_norm(x.data_ptr(), wq.packed_mma.data_ptr(), wq.scales.data_ptr(),
+                                            y.data_ptr(), n, k, 128, res2.data_ptr(), ln.data_ptr(), h2.data_ptr(),
+                                            1e-6, c2.data_ptr(), _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(res, res2) and torch.equal(h1, h2)
+    assert epoch.item() == 1 and lib.lb_device_error() == 0
+
+
+def test_tp_gemv_allreduce_norm_wait_runs_out_and_reports():
+    """A peer that never publishes: the last CTA gives up after about a second, the status word reads 2, the epoch
+    does not advance, the counter is left zero and the context stays usable."""
+    n, k, lib = 896, 896, _lib()
+    wq = _w4(n, k, 1)
+    x = torch.ones(1, k, device="cuda").half()
+    res, ln, h = (torch.zeros(n, device="cuda").half(), torch.ones(n, device="cuda").half(),
+                  torch.empty(n, device="cuda").half())
+    mine = torch.zeros(32 + 2 * n, device="cuda", dtype=torch.int64)
+    peer = torch.zeros(32 + 2 * n, device="cuda", dtype=torch.int64)
+    bufs = torch.tensor([mine.data_ptr(), peer.data_ptr()], dtype=torch.int64, device="cuda")
+    epoch = torch.zeros(1, device="cuda", dtype=torch.int32)
+    counter = torch.zeros(1, device="cuda", dtype=torch.int32)
+    lib.lb_clear_device_error()
+    assert _fused_ar_call(lib, x, wq, None, n, bufs, epoch, 0, 2, res, ln, h, counter) == 0
+    torch.cuda.synchronize()
+    assert lib.lb_device_error() == 2
+    assert epoch.item() == 0 and counter.item() == 0
+    lib.lb_clear_device_error()
+    assert lib.lb_device_error() == 0
+    assert torch.isfinite((x + 1).float()).all()
+
+
 def test_decode_gemv_fusable_rule():
     assert _lib().lb_decode_gemv_fusable(2048, 11008) == 1      # 3B down: 86 chunks over 16 warps
     assert _lib().lb_decode_gemv_fusable(3584, 18944) == 0      # 7B down on one GPU: longer than one CTA holds

@@ -60,9 +60,10 @@ def _rank(rank, world, port, results, fuse=()):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("fuse", [(), ("epilogue",)])
+@pytest.mark.parametrize("fuse", [(), ("epilogue",), ("epilogue", "gemv_allreduce")])
 def test_tp2_decoder_matches_single_gpu(fuse):
-    """fuse=("epilogue",): the residual add + RMSNorm run inside the one-shot allreduce"""
+    """fuse=("epilogue",): the residual add + RMSNorm run inside the one-shot allreduce; + "gemv_allreduce": the o
+    and down GEMVs push their tiles to every rank and sum, add and normalize in their last CTA"""
     world = 2
     results = mp.get_context("spawn").Manager().dict()
     mp.start_processes(_rank, args=(world, _free_port(), results, fuse), nprocs=world, start_method="spawn")
