@@ -11,8 +11,9 @@ by time.
   value   whole-job GB/s with everything resident in HBM: K steps captured as CUDA graphs (one kernel launch per
           call, programmatic dependent launch between them), timed with CUDA events on the launching stream,
           max over ranks;
-  e2e     the same metric through the public API (lowbit.ops.linear), eager, with each call's activation copied
-          from pinned host memory to the GPU and its output copied back inside the timed region;
+  e2e     the same metric through the public API (lowbit.ops.linear), eager, with each step's activations copied
+          from pinned host memory to the GPU (one copy) and its outputs copied back (one copy) inside the timed
+          region, the stream synchronized at the end of every step;
   cpu_baseline / --impl reference
           the reference's CPU path (dequantize on CPU tensors + fp32 F.linear, lowbit/ops.py:119-123) restated in
           oracle/oracle.py, timed on the host cores of this machine.
@@ -21,6 +22,7 @@ Under torchrun (--gpus N > 1) each rank runs the same sweep on its own GPU (the 
 exchange step: replicas, weak scaling); value sums all ranks' bytes over the slowest rank's time.
 """
 import argparse
+import itertools
 import json
 import os
 import pathlib
@@ -298,17 +300,24 @@ def run_ours(args, rank, world, local):
     value = world * step_bytes * args.steps / (ms * 1e-3) / 1e9
     ms_per_step = ms / args.steps
 
-    # e2e: the public API, eager, host buffers in and out every call
-    xs_host = [x.cpu().pin_memory() for x in xs]
-    ys_host = [torch.empty(1, n, dtype=torch.half).pin_memory() for _, _, _, n in projs]
-    h2d = sum(x.numel() * 2 for x in xs_host)
-    d2h = sum(y.numel() * 2 for y in ys_host)
+    # e2e: the public API (lowbit.ops.linear), eager, from pinned host memory and back every step: one host-to-
+    # device copy of the step's 21 activation rows, the 21 calls writing into one device buffer, one copy of the 21
+    # outputs back to the host, then a synchronize
+    ks, ns = [k for _, _, k, _ in projs], [n for _, _, _, n in projs]
+    x_host = torch.cat([x.reshape(-1).cpu() for x in xs]).pin_memory()
+    y_host = torch.empty(sum(ns), dtype=torch.half).pin_memory()
+    x_dev = torch.empty(sum(ks), dtype=torch.half, device=device)
+    y_dev = torch.empty(sum(ns), dtype=torch.half, device=device)
+    x_views = [x_dev[a:a + k].view(1, k) for a, k in zip(itertools.accumulate([0] + ks[:-1]), ks)]
+    y_views = [y_dev[a:a + n].view(1, n) for a, n in zip(itertools.accumulate([0] + ns[:-1]), ns)]
+    h2d, d2h = x_host.numel() * 2, y_host.numel() * 2
     e2e_steps = max(3, min(args.steps, 200))
 
     def e2e_step(layer):
-        for xh, yh, wq in zip(xs_host, ys_host, layer):
-            xd = xh.to(device, non_blocking=True)
-            yh.copy_(ops.linear(xd, wq), non_blocking=True)
+        x_dev.copy_(x_host, non_blocking=True)
+        for xv, yv, wq in zip(x_views, y_views, layer):
+            ops.linear(xv, wq, out=yv)
+        y_host.copy_(y_dev, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     for i in range(3):
         e2e_step(sets[i % n_sets])
@@ -379,8 +388,9 @@ def run_ours(args, rank, world, local):
         "clocks": clocks,
         "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps,
-                "how": "lowbit.ops.linear eager per call; pinned-host x -> GPU and y -> pinned host inside the "
-                       "timed region; stream synchronized at the end of each step"},
+                "how": "lowbit.ops.linear eager per call (out= slices of one device buffer); the step's 21 "
+                       "activation rows pinned-host -> GPU in one copy and its 21 outputs -> pinned host in one "
+                       "copy inside the timed region; stream synchronized at the end of each step"},
         "gpu_launches": launches_per_step * args.steps,
     }
     if shapes is not None:

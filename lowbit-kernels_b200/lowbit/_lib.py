@@ -84,6 +84,15 @@ def _check(x, w, s, group):
         raise RuntimeError("shape mismatch")
 
 
+def _out(out, m, n, device):
+    """The output tensor: a new [m, n] fp16 tensor, or `out` after checking that it is one."""
+    if out is None:
+        return torch.empty((m, n), dtype=torch.float16, device=device)
+    if out.shape != (m, n) or out.dtype != torch.float16 or out.device != device or not out.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous float16 [{m}, {n}] tensor on {device}")
+    return out
+
+
 class _Device:
     """Make `dev` the current CUDA device for one call (the reference's CUDAGuard), cheaply."""
     __slots__ = ("dev", "prev")
@@ -121,10 +130,10 @@ class Ext:
     def get_option(self, name):
         return self.lib.lb_get_option(OPTIONS[name])
 
-    def w4_gemv(self, x, w, s, group, version, rows_per_warp=0):
+    def w4_gemv(self, x, w, s, group, version, rows_per_warp=0, out=None):
         _check(x, w, s, group)
         m, k, n = x.shape[0], x.shape[1], w.shape[0]
-        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+        y = _out(out, m, n, x.device)
         with _Device(x.device):
             rc = self.lib.lb_w4_gemv(x.data_ptr(), w.data_ptr(), s.data_ptr(), y.data_ptr(), m, n, k, group,
                                      int(version), int(rows_per_warp), torch.cuda.current_stream().cuda_stream)
@@ -132,10 +141,10 @@ class Ext:
             self._raise(rc)
         return y
 
-    def w4_gemm_tc(self, x, w, s, group, row_tiles=0):
+    def w4_gemm_tc(self, x, w, s, group, row_tiles=0, out=None):
         _check(x, w, s, group)
         m, k, n = x.shape[0], x.shape[1], w.shape[0]
-        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+        y = _out(out, m, n, x.device)
         with _Device(x.device):
             rc = self.lib.lb_w4_gemm_tc(x.data_ptr(), w.data_ptr(), s.data_ptr(), y.data_ptr(), m, n, k, group,
                                         int(row_tiles), torch.cuda.current_stream().cuda_stream)

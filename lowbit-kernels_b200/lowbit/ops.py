@@ -92,17 +92,18 @@ NEEDS = {1: "packed", 2: "packed", 3: "packed_v3", 4: "packed_v3", 5: "packed_mm
 MAX_ROWS = {1: 8, 2: 8, 3: 8, 4: 8, 5: 64, 6: 8}
 
 
-def gemv(x, wq, version=4, rows_per_warp=0):
+def gemv(x, wq, version=4, rows_per_warp=0, out=None):
     """x [M, K] fp16 -> [M, N] fp16. Versions 1-4 and 6: M <= 8; version 5: M <= 64 (tensor cores).
-    Versions 5 and 6 read the same layout (packed_mma), so a model needs only that copy."""
+    Versions 5 and 6 read the same layout (packed_mma), so a model needs only that copy. `out`: an optional
+    contiguous fp16 [M, N] tensor the result is written into (no allocation)."""
     if version not in NEEDS:
         raise ValueError(f"version must be one of {sorted(NEEDS)}")
     if getattr(wq, NEEDS[version]) is None:
         raise ValueError(f"v{version} reads {NEEDS[version]}, which this W4Weight does not keep")
     if version == 5:
-        return ext().w4_gemm_tc(x.contiguous(), wq.packed_mma, wq.scales, wq.group, rows_per_warp)
+        return ext().w4_gemm_tc(x.contiguous(), wq.packed_mma, wq.scales, wq.group, rows_per_warp, out=out)
     w = wq.packed_mma if version == 6 else wq.packed_v3 if version >= 3 else wq.packed
-    return ext().w4_gemv(x.contiguous(), w, wq.scales, wq.group, version, rows_per_warp)
+    return ext().w4_gemv(x.contiguous(), w, wq.scales, wq.group, version, rows_per_warp, out=out)
 
 
 def quantize_w4_gpu(w, group=128, clip_grid=None, rows_per_pass=2048):
@@ -190,13 +191,14 @@ def auto_version(m, wq):
     return None
 
 
-def linear(x, wq, max_gemv_rows=8, version=0):
+def linear(x, wq, max_gemv_rows=8, version=0, out=None):
     """Decode (few rows): an INT4 kernel; prefill (many rows): dequantize, then cuBLAS fp16 GEMM. version 0 =
     auto_version; a fixed version runs up to min(max_gemv_rows, its row limit) rows (version 5: 64), and
-    dequantize + cuBLAS above that (lowbit/ops.py:163-178)."""
+    dequantize + cuBLAS above that (lowbit/ops.py:163-178). `out` (an addition to the reference's signature): an
+    optional contiguous fp16 [M, N] tensor that receives the result."""
     m = x.shape[0]
     if m == 0:
-        return x.new_empty(0, wq.n)
+        return x.new_empty(0, wq.n) if out is None else out
     if version == 0:
         v = auto_version(m, wq)
     elif version in MAX_ROWS:
@@ -204,5 +206,10 @@ def linear(x, wq, max_gemv_rows=8, version=0):
     else:
         raise ValueError(f"version must be 0 (auto) or one of {sorted(MAX_ROWS)}")
     if v is not None:
-        return gemv(x, wq, v)
-    return torch.nn.functional.linear(x, dequant(wq, "mma" if wq.packed_mma is not None else "canonical"))
+        return gemv(x, wq, v) if out is None else gemv(x, wq, v, out=out)
+    y = torch.nn.functional.linear(x, dequant(wq, "mma" if wq.packed_mma is not None else "canonical"))
+    if out is None:
+        return y
+    if out.shape != y.shape or out.dtype != y.dtype:
+        raise RuntimeError(f"out must be a float16 {tuple(y.shape)} tensor")
+    return out.copy_(y)

@@ -21,7 +21,8 @@ def weight(n=1024, k=256, layouts=("mma",)):
 @pytest.fixture
 def calls(monkeypatch):
     seen = []
-    monkeypatch.setattr(ops, "gemv", lambda x, wq, v, rpw=0: seen.append(v) or torch.zeros(x.shape[0], wq.n))
+    monkeypatch.setattr(ops, "gemv", lambda x, wq, v, rpw=0, out=None: seen.append(v) or
+                        (torch.zeros(x.shape[0], wq.n) if out is None else out))
     monkeypatch.setattr(ops, "dequant", lambda wq, layout=None: seen.append("dequant") or torch.zeros(wq.n, wq.k))
     return seen
 
@@ -70,6 +71,12 @@ def test_a_fixed_version_never_passes_its_row_limit(calls):
     ops.linear(torch.zeros(64, 256), weight(), version=5)
     ops.linear(torch.zeros(65, 256), weight(), version=5)
     assert calls == ["dequant", 5, "dequant"]
+
+
+def test_out_is_forwarded_and_returned(calls):
+    buf = torch.empty(1, 1024)
+    assert ops.linear(torch.zeros(1, 256), weight(), out=buf) is buf
+    assert calls == [6]
 
 
 def test_bad_versions_and_empty_input(calls):

@@ -283,6 +283,21 @@ def test_dispatch_matrix():
             assert err <= NORM_BOUND, (name, m, err)
 
 
+def test_linear_out_writes_in_place_with_the_same_bits():
+    """out= (used by the end-to-end benchmark): the result lands in the given slice of a larger buffer, bit-equal to
+    the allocating call, for the INT4 kernels and the dequantize + cuBLAS path; a wrong buffer is refused."""
+    wq = ops.W4Weight.from_float(torch.randn(1000, 1536))
+    buf = torch.full((3000,), float("nan"), device="cuda").half()
+    for m in (1, 3, 20, 70):
+        x = torch.randn(m, 1536).half().cuda()
+        out = torch.empty(m, 1000, device="cuda").half() if m > 1 else buf[1000:2000].view(1, 1000)
+        assert ops.linear(x, wq, out=out) is out
+        assert torch.equal(out, ops.linear(x, wq))
+    assert torch.isnan(buf[:1000].float()).all() and torch.isnan(buf[2000:].float()).all()
+    with pytest.raises(RuntimeError):
+        ops.linear(torch.randn(1, 1536).half().cuda(), wq, out=torch.empty(1, 999, device="cuda").half())
+
+
 def test_fixed_version_past_its_limit_falls_back():
     wq = ops.W4Weight.from_float(torch.randn(256, 512))
     x = torch.randn(9, 512).half().cuda()
