@@ -64,8 +64,9 @@ LB_API const char* lb_status_string(int status);
 /* message of the last failed call on this host thread ("" after a successful call) */
 LB_API const char* lb_last_error(void);
 
-/* Device-side status of the current device: nonzero when a kernel's bounded wait gave up (a kernel bug, never
- * expected), in which case that kernel's output is undefined. Synchronizes the device. */
+/* Device-side status of the current device: nonzero when a kernel's bounded wait gave up (1: a pipeline barrier,
+ * a kernel bug, never expected; 2: a peer rank's epoch, tensor parallelism) or a decode position read from device
+ * memory lay outside the KV cache (3); that kernel's output is then undefined. Synchronizes the device. */
 LB_API int lb_device_error(void);
 LB_API void lb_clear_device_error(void);
 
@@ -132,7 +133,10 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  *                      k, v appended to the caches [nkv, max_len, hd] at row pos; then one query token attends
  *                      to rows 0..pos (grouped heads, nh % nkv == 0, scale 1/sqrt(hd)) -> out [nh, hd].
  *                      part_o (fp32, nh * lb_decode_attention_splits(max_len) * hd) and part_ml (fp32, twice
- *                      nh * splits) are caller-owned scratch; caches and part_o 16-byte aligned
+ *                      nh * splits) are caller-owned scratch; caches and part_o 16-byte aligned; hd a multiple of
+ *                      8 (<= 1024), max_len <= 65536; the cache rows below pos are read before the kernel waits on
+ *                      the previous kernel in the stream (they must not be its output); a pos outside
+ *                      0..max_len-1 writes nothing and sets lb_device_error() to 3
  * lb_decode_silu_mul:  a[I] = fp16(silu(gu[i])) * gu[I + i]     (gu = [gate | up])
  */
 LB_API int lb_decode_embed(const void* emb, const int64_t* tok, void* x, int64_t H, lb_stream_t stream);

@@ -224,13 +224,15 @@ const char* lb_last_error(void) { return g_err; }
 int lb_device_error(void) {
   int a = lb::device_error();
   if (!a) a = lb::gemm_tc_device_error();
-  return a ? a : lb::allreduce_device_error();
+  if (!a) a = lb::allreduce_device_error();
+  return a ? a : lb::decode_device_error();
 }
 
 void lb_clear_device_error(void) {
   lb::clear_device_error();
   lb::gemm_tc_clear_device_error();
   lb::allreduce_clear_device_error();
+  lb::decode_clear_device_error();
 }
 
 int lb_set_option(int option, int value) {
@@ -363,8 +365,13 @@ int lb_decode_rmsnorm(void* x, const void* r, const void* w, void* h, int64_t H,
 
 static int check_heads(int nh, int nkv, int hd, int64_t max_len) {
   if (nh <= 0 || nkv <= 0 || nh % nkv) return fail(LB_ERR_ARGUMENT, "head counts %d / %d", nh, nkv);
-  if (hd <= 0 || hd % 2 || hd > 1024) return fail(LB_ERR_ARGUMENT, "head dim %d must be even and <= 1024", hd);
-  if (max_len <= 0 || max_len > (1 << 24)) return fail(LB_ERR_ARGUMENT, "bad cache length %lld", (long long)max_len);
+  if (hd <= 0 || hd % 8 || hd > 1024)
+    return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8 and <= 1024", hd);
+  if (max_len <= 0 || max_len > lb::attn_max_len())
+    return fail(LB_ERR_ARGUMENT, "cache length %lld must be in 1..%d", (long long)max_len, lb::attn_max_len());
+  if (lb::attn_smem_bytes(nh, nkv, hd) > 227 * 1024)
+    return fail(LB_ERR_UNSUPPORTED, "%d query heads per kv head at head dim %d need more shared memory than a CTA has",
+                nh / nkv, hd);
   return 0;
 }
 

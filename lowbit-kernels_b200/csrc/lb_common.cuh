@@ -116,6 +116,7 @@ namespace lb {
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrBarrierTimeout = 1;
 constexpr int kErrPeerTimeout = 2;    // a peer rank did not publish its epoch in time (allreduce)
+constexpr int kErrBadPosition = 3;   // a decode position outside the KV cache (nothing was read or written)
 
 // ------------------------------------------------------------------------------------- peer-memory epochs
 // Row-parallel sums over NVLink peer memory: every rank owns a peer-mapped buffer that starts with
@@ -149,6 +150,14 @@ __device__ __forceinline__ bool wait_peer_epoch(const uint32_t* f, uint32_t e, i
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// 16-byte global -> shared copy through L2 only (no L1 allocation), completed by cp_async_wait<N>
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");

@@ -89,13 +89,21 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(__half* __restrict
 
 // Split attention for one query token, fused with the q|k|v epilogue. CTA (kv head, split) takes cache positions
 // [64 s, 64 s + 64) that are <= pos:
+//   * the range's cached K and V rows (< pos, written by earlier steps) are copied into shared memory with
+//     cp.async before the kernel waits on its predecessor, so their HBM latency overlaps the q|k|v projection;
 //   * q of the group's heads = RoPE(qkv + bias) (rotate-half pairing: dims j and j + hd/2, angle pos *
 //     inv_freq[j]), in fp32 shared memory, pre-multiplied by the softmax scale;
 //   * the CTA whose range holds pos also rotates k, and writes k and v (+ bias) into the caches at row pos;
-//   * the range's K and V rows are staged in shared memory with 16-byte loads (row pos from the values just made);
+//   * scores: one thread per (head, position), a full hd-long dot product (a warp = one head's 32 positions, so
+//     q reads broadcast; K rows are padded by 16 bytes so the 32 rows a warp reads sit on distinct banks);
 //   * writes the split's running max, sum of exponentials and unnormalized output (fp32) for attn_combine_kernel.
 constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 256;
+
+__host__ __device__ constexpr int attn_k_stride(int hd) { return hd + 8; }
+
+// status word of the decode kernels (a position outside the cache); read by decode_device_error()
+__device__ int g_decode_status;
 
 __device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& ra, float& rb) {
   ra = a * c - b * s;
@@ -111,31 +119,41 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
                                                                   int max_len, float scale) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
   pdl_launch_dependents();
-  pdl_wait();
   const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
   const int g = nh / nkv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32, half = hd / 2;
-  const int pos = (int)*pos_p, L = pos + 1;
+  const int ks = attn_k_stride(hd);
+  // the position and the cached rows below it were written by earlier steps, before this step's kernels
+  const int64_t pos64 = *pos_p;
+  if (pos64 < 0 || pos64 >= max_len) {   // nothing is read or written outside the caches
+    if (threadIdx.x == 0) atomicExch(&g_decode_status, kErrBadPosition);
+    pdl_wait();
+    return;
+  }
+  const int pos = (int)pos64, L = pos + 1;
   const int p0 = split * kAttnChunk, np = min(kAttnChunk, L - p0);
   const size_t pbase = ((size_t)kvh * nsplit + split) * g;
   if (np <= 0) {   // nothing cached here yet: an empty partial
+    pdl_wait();
     for (int i = threadIdx.x; i < g; i += blockDim.x) {
       part_ml[(pbase + i) * 2] = -INFINITY;
       part_ml[(pbase + i) * 2 + 1] = 0.f;
     }
     return;
   }
-  __half* sk = reinterpret_cast<__half*>(sm_raw);               // [64][hd]
-  __half* sv = sk + kAttnChunk * hd;                             // [64][hd]
+  __half* sk = reinterpret_cast<__half*>(sm_raw);               // [64][ks]
+  __half* sv = sk + kAttnChunk * ks;                             // [64][hd]
   float* sq = reinterpret_cast<float*>(sv + kAttnChunk * hd);    // [g][hd]
   float* ss = sq + g * hd;                                       // [g][64]
-  // cached rows (those < pos) of the range
   const int ncached = min(np, pos - p0), vec = hd / 8;
-  const uint4* kg = reinterpret_cast<const uint4*>(kc + ((size_t)kvh * max_len + p0) * hd);
-  const uint4* vg = reinterpret_cast<const uint4*>(vc + ((size_t)kvh * max_len + p0) * hd);
+  const __half* kg = kc + ((size_t)kvh * max_len + p0) * hd;
+  const __half* vg = vc + ((size_t)kvh * max_len + p0) * hd;
   for (int i = threadIdx.x; i < ncached * vec; i += blockDim.x) {
-    reinterpret_cast<uint4*>(sk)[i] = kg[i];
-    reinterpret_cast<uint4*>(sv)[i] = vg[i];
+    const int r = i / vec, c8 = (i - r * vec) * 8;
+    cp_async16(smem_addr(sk + r * ks + c8), kg + (size_t)r * hd + c8);
+    cp_async16(smem_addr(sv + r * hd + c8), vg + (size_t)r * hd + c8);
   }
+  cp_async_commit();
+  pdl_wait();   // qkv comes from the previous kernel in the stream
   // q of the group's heads, and (in the range holding pos) this token's k and v
   const bool mine = pos < p0 + kAttnChunk;
   for (int i = threadIdx.x; i < (g + (mine ? 2 : 0)) * half; i += blockDim.x) {
@@ -164,38 +182,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       sq[hh * hd + j] = __half2float(ha) * scale;
       sq[hh * hd + j + half] = __half2float(hb) * scale;
     } else {
-      sk[(pos - p0) * hd + j] = ha;
-      sk[(pos - p0) * hd + j + half] = hb;
+      sk[(pos - p0) * ks + j] = ha;
+      sk[(pos - p0) * ks + j + half] = hb;
       kc[((size_t)kvh * max_len + pos) * hd + j] = ha;
       kc[((size_t)kvh * max_len + pos) * hd + j + half] = hb;
     }
   }
+  cp_async_wait<0>();
   __syncthreads();
-  // scores: warp per position, lane over 4 consecutive dims of every query head of the group. Every lane runs the
-  // same number of 128-dim rounds (lanes past hd contribute zero), so the full-warp reductions are reached by all
-  // 32 lanes whatever hd is.
-  for (int p = warp; p < np; p += nw) {
-    for (int base = 0; base < hd; base += 128) {
-      const int e0 = base + lane * 4;
-      const bool in = e0 < hd;
-      float2 k01 = make_float2(0.f, 0.f), k23 = make_float2(0.f, 0.f);
-      if (in) {
-        const uint2 kr = *reinterpret_cast<const uint2*>(sk + p * hd + e0);
-        k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
-        k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+  // scores: thread (head h, position p), the whole dot product in fp32
+  for (int i = threadIdx.x; i < g * kAttnChunk; i += blockDim.x) {
+    const int h = i / kAttnChunk, p = i - h * kAttnChunk;
+    if (p < np) {
+      const float* q = sq + h * hd;
+      const __half* k = sk + p * ks;
+      float d0 = 0.f, d1 = 0.f;
+      for (int e = 0; e < hd; e += 8) {
+        const uint4 kr = *reinterpret_cast<const uint4*>(k + e);
+        const float4 qa = *reinterpret_cast<const float4*>(q + e);
+        const float4 qb = *reinterpret_cast<const float4*>(q + e + 4);
+        const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+        const float2 f0 = __half22float2(kh[0]), f1 = __half22float2(kh[1]);
+        const float2 f2 = __half22float2(kh[2]), f3 = __half22float2(kh[3]);
+        d0 = fmaf(qa.x, f0.x, d0);
+        d1 = fmaf(qa.y, f0.y, d1);
+        d0 = fmaf(qa.z, f1.x, d0);
+        d1 = fmaf(qa.w, f1.y, d1);
+        d0 = fmaf(qb.x, f2.x, d0);
+        d1 = fmaf(qb.y, f2.y, d1);
+        d0 = fmaf(qb.z, f3.x, d0);
+        d1 = fmaf(qb.w, f3.y, d1);
       }
-      for (int h = 0; h < g; ++h) {
-        float d = 0.f;
-        if (in) {
-          const float4 qv = *reinterpret_cast<const float4*>(sq + h * hd + e0);
-          d = qv.x * k01.x + qv.y * k01.y + qv.z * k23.x + qv.w * k23.y;
-        }
-        d = warp_sum(d);
-        if (lane == 0) {
-          if (base == 0) ss[h * kAttnChunk + p] = d;
-          else ss[h * kAttnChunk + p] += d;
-        }
-      }
+      ss[h * kAttnChunk + p] = d0 + d1;
     }
   }
   __syncthreads();
@@ -237,24 +255,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
   }
 }
 
-// out[head] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s; grid nh, block hd
+// out[head] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s; grid nh, block hd. The splits' (m, l) pairs are
+// read once into shared memory (in parallel), warp 0 turns them into weights exp(m_s - M) (0 for empty splits)
+// and their weighted sum, and the hd-long partial rows are read with independent loads.
+constexpr int kCombineMaxSplits = 1024;
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, __half* out, int nh, int nkv, int hd,
                                     int nsplit) {
+  __shared__ float sw[kCombineMaxSplits], sl[kCombineMaxSplits];
+  __shared__ float s_den;
   pdl_launch_dependents();
   pdl_wait();
   const int head = blockIdx.x, e = threadIdx.x, g = nh / nkv, kvh = head / g, h = head - kvh * g;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(((size_t)kvh * nsplit + s) * g + h) * 2]);
-  float num = 0.f, den = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const size_t b = ((size_t)kvh * nsplit + s) * g + h;
-    const float m = part_ml[b * 2];
-    if (m == -INFINITY) continue;
-    const float w = expf(m - M);
-    den += w * part_ml[b * 2 + 1];
-    num += w * part_o[b * hd + e];
+  for (int s = threadIdx.x; s < nsplit; s += blockDim.x) {
+    const float2 v = *reinterpret_cast<const float2*>(part_ml + (((size_t)kvh * nsplit + s) * g + h) * 2);
+    sw[s] = v.x;
+    sl[s] = v.y;
   }
-  out[(size_t)head * hd + e] = __float2half_rn(num / den);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, sw[s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float den = 0.f;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float m = sw[s];
+      const float w = m == -INFINITY ? 0.f : expf(m - M);
+      sw[s] = w;
+      den += w * sl[s];
+    }
+    den = warp_sum(den);
+    if (lane == 0) s_den = den;
+  }
+  __syncthreads();
+  float num = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < nsplit; ++s) {
+    const float w = sw[s];
+    if (w != 0.f) num += w * part_o[(((size_t)kvh * nsplit + s) * g + h) * hd + e];
+  }
+  out[(size_t)head * hd + e] = __float2half_rn(num / s_den);
 }
 
 // a = fp16(fp16(silu(g)) * u) from the fused [gate | up] projection output (act_fn(gate) * up in fp16)
@@ -301,9 +342,23 @@ int rmsnorm_max_hidden() { return 8 * kRmsThreads * kRmsVec; }
 
 int attn_splits(int max_len) { return (max_len + kAttnChunk - 1) / kAttnChunk; }
 
+int attn_max_len() { return kAttnChunk * kCombineMaxSplits; }
+
+int decode_device_error() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_decode_status, sizeof(int));
+  return v;
+}
+
+void decode_clear_device_error() {
+  int z = 0;
+  cudaMemcpyToSymbol(g_decode_status, &z, sizeof(int));
+}
+
 size_t attn_smem_bytes(int nh, int nkv, int hd) {
   const int g = nh / nkv;
-  return (size_t)2 * kAttnChunk * hd * sizeof(__half) + (size_t)(g * hd + g * kAttnChunk) * sizeof(float);
+  return (size_t)kAttnChunk * (attn_k_stride(hd) + hd) * sizeof(__half) +
+         (size_t)(g * hd + g * kAttnChunk) * sizeof(float);
 }
 
 cudaError_t launch_attention(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,

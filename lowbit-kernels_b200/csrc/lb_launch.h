@@ -90,6 +90,9 @@ cudaError_t launch_embed(const __half* emb, const int64_t* tok, __half* x, int H
 cudaError_t launch_rmsnorm(__half* x, const __half* r, const __half* w, __half* h, int H, float eps, cudaStream_t st);
 int rmsnorm_max_hidden();
 int attn_splits(int max_len);
+int attn_max_len();   // longest cache the split attention and its combine step take
+int decode_device_error();
+void decode_clear_device_error();
 size_t attn_smem_bytes(int nh, int nkv, int hd);
 cudaError_t launch_attention(const __half* qkv, const __half* bias, const float* inv_freq, const int64_t* pos,
                              __half* kc, __half* vc, float* part_o, float* part_ml, __half* out, int nh, int nkv,

@@ -118,11 +118,11 @@ def _rope(t, pos, inv_freq):
     return torch.cat([a * c - b * s, b * c + a * s], -1)
 
 
-@pytest.mark.parametrize("pos", [0, 63, 64, 257])
+@pytest.mark.parametrize("pos", [0, 63, 64, 257, 3000])
 @pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64)])
 def test_fused_attention_kernel(pos, heads):
     nh, nkv, hd = heads
-    max_len = 320
+    max_len = 320 if pos < 320 else 4096     # 3000: 47 splits hold cached rows, 17 are empty
     g = torch.Generator(device="cuda").manual_seed(pos + nh)
     qkv = torch.randn((nh + 2 * nkv) * hd, device="cuda", generator=g).half()
     bias = (0.1 * torch.randn((nh + 2 * nkv) * hd, device="cuda", generator=g)).half()
@@ -155,6 +155,29 @@ def test_fused_attention_kernel(pos, heads):
     att = torch.softmax((q[:, None, :] @ Kx.transpose(1, 2))[:, 0] / hd ** 0.5, -1)
     want = (att[:, None, :] @ Vx)[:, 0]
     assert torch.allclose(out.float().view(nh, hd), want, atol=3e-3, rtol=3e-3)
+
+
+def test_attention_position_outside_the_cache_writes_nothing():
+    """pos lives in device memory, so the host cannot check it: a pos >= max_len makes every CTA return before any
+    read or write, and the status word reads 3."""
+    lib, nh, nkv, hd, max_len = _lib(), 16, 2, 128, 128
+    qkv = torch.randn((nh + 2 * nkv) * hd, device="cuda").half()
+    kc, vc = torch.randn(nkv, max_len, hd, device="cuda").half(), torch.randn(nkv, max_len, hd, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    inv_freq = torch.ones(hd // 2, device="cuda")
+    splits = lib.lb_decode_attention_splits(max_len)
+    part_o, part_ml = torch.empty(nh * splits * hd, device="cuda"), torch.empty(nh * splits * 2, device="cuda")
+    out = torch.zeros(nh * hd, device="cuda").half()
+    lib.lb_clear_device_error()
+    p = torch.tensor([max_len], device="cuda")
+    assert lib.lb_decode_attention(qkv.data_ptr(), None, inv_freq.data_ptr(), p.data_ptr(), kc.data_ptr(),
+                                   vc.data_ptr(), part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr(), nh, nkv, hd,
+                                   max_len, _stream()) == 0
+    torch.cuda.synchronize()
+    assert lib.lb_device_error() == 3
+    assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
+    lib.lb_clear_device_error()
+    assert lib.lb_device_error() == 0
 
 
 def test_silu_mul_kernel():

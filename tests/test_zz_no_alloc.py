@@ -21,6 +21,18 @@ def test_noalloc_refuses_calls_larger_than_its_scratch():
     assert "scratch" in msg and "262144" in msg and "lb_decode_attention" in msg
 
 
+def test_attention_refuses_shapes_its_kernels_do_not_take():
+    """head dims that are not a multiple of 8, caches longer than 65536 rows and head groups whose tiles exceed a
+    CTA's shared memory fail with a message before touching the device (fake, aligned pointers; no GPU needed)."""
+    lib = _lib.load_library()
+    p = 0x10000
+    call = lambda nh, nkv, hd, max_len: lib.lb_decode_attention(p, None, p, p, p, p, p, p, p, nh, nkv, hd, max_len,
+                                                                None)
+    assert call(16, 2, 12, 1024) == LB_ERR_ARGUMENT and "multiple of 8" in lib.lb_last_error().decode()
+    assert call(16, 2, 128, 65537) == LB_ERR_ARGUMENT and "65536" in lib.lb_last_error().decode()
+    assert call(128, 1, 1024, 1024) == 3 and "shared memory" in lib.lb_last_error().decode()   # LB_ERR_UNSUPPORTED
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128)])
 def test_noalloc_matches_caller_scratch_on_two_calls_in_a_row(heads):
