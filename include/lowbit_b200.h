@@ -133,7 +133,8 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  *                      k, v appended to the caches [nkv, max_len, hd] at row pos; then one query token attends
  *                      to rows 0..pos (grouped heads, nh % nkv == 0, scale 1/sqrt(hd)) -> out [nh, hd].
  *                      part_o (fp32, nh * lb_decode_attention_splits(max_len) * hd) and part_ml (fp32, twice
- *                      nh * splits) are caller-owned scratch; caches and part_o 16-byte aligned; hd a multiple of
+ *                      nh * splits) are caller-owned scratch; qkv, bias, inv_freq, the caches and part_o 16-byte
+ *                      aligned, part_ml 8-byte aligned; hd a multiple of
  *                      8 (<= 1024), max_len <= 65536; the cache rows below pos are read before the kernel waits on
  *                      the previous kernel in the stream (they must not be its output); a pos outside
  *                      0..max_len-1 writes nothing and sets lb_device_error() to 3

@@ -375,6 +375,15 @@ static int check_heads(int nh, int nkv, int hd, int64_t max_len) {
   return 0;
 }
 
+// the attention kernels read qkv and bias with 8-byte vectors, inv_freq and the caches with 16-byte ones
+static int check_attention_alignment(const void* qkv, const void* bias, const void* inv_freq, const void* kc,
+                                     const void* vc) {
+  if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(inv_freq) |
+        reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15u) != 0)
+    return fail(LB_ERR_ALIGNMENT, "qkv, bias, inv_freq and the caches must be 16-byte aligned");
+  return 0;
+}
+
 int lb_decode_attention_splits(int64_t max_len) { return max_len > 0 ? lb::attn_splits((int)max_len) : 0; }
 
 int lb_decode_attention(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos, void* k_cache,
@@ -384,11 +393,9 @@ int lb_decode_attention(const void* qkv, const void* bias, const float* inv_freq
     return fail(LB_ERR_ARGUMENT, "null pointer argument");
   int rc = check_heads(nh, nkv, hd, max_len);
   if (rc) return rc;
-  if (hd % 8) return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8", hd);
-  if (lb::attn_smem_bytes(nh, nkv, hd) > 200 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
-  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
-        reinterpret_cast<uintptr_t>(part_o)) & 15u) != 0)
-    return fail(LB_ERR_ALIGNMENT, "caches and part_o must be 16-byte aligned");
+  if ((rc = check_attention_alignment(qkv, bias, inv_freq, k_cache, v_cache))) return rc;
+  if (((reinterpret_cast<uintptr_t>(part_o) & 15u) | (reinterpret_cast<uintptr_t>(part_ml) & 7u)) != 0)
+    return fail(LB_ERR_ALIGNMENT, "part_o must be 16-byte and part_ml 8-byte aligned");
   if ((rc = check_device())) return rc;
   return launched(lb::launch_attention(static_cast<const __half*>(qkv), static_cast<const __half*>(bias), inv_freq, pos,
                                        static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), part_o, part_ml,
@@ -403,7 +410,6 @@ int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* 
   if (!qkv || !inv_freq || !pos || !k_cache || !v_cache || !out) return fail(LB_ERR_ARGUMENT, "null pointer argument");
   int rc = check_heads(nh, nkv, hd, max_len);
   if (rc) return rc;
-  if (hd % 8) return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8", hd);
   const size_t splits = (size_t)lb::attn_splits((int)max_len);
   const size_t need = (size_t)nh * splits * (size_t)(hd + 2);
   if (need > lb::kNoAllocScratchFloats)
@@ -411,9 +417,7 @@ int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* 
                 "lb_decode_attention_noalloc needs %zu floats of scratch (%d heads x %zu splits x (%d + 2)); the "
                 "library holds %zu -- pass caller-owned scratch to lb_decode_attention instead",
                 need, nh, splits, hd, lb::kNoAllocScratchFloats);
-  if (lb::attn_smem_bytes(nh, nkv, hd) > 200 * 1024) return fail(LB_ERR_UNSUPPORTED, "query group too large");
-  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) != 0)
-    return fail(LB_ERR_ALIGNMENT, "caches must be 16-byte aligned");
+  if ((rc = check_attention_alignment(qkv, bias, inv_freq, k_cache, v_cache))) return rc;
   if ((rc = check_device())) return rc;
   float* scratch = lb::noalloc_attn_scratch();
   if (!scratch) return fail(LB_ERR_CUDA, "could not resolve the attention scratch on this device");

@@ -110,15 +110,18 @@ __device__ __forceinline__ void rope_pair(float a, float b, float c, float s, fl
   rb = b * c + a * s;
 }
 
+// HD: the head dimension when it is a compile-time constant (64, 128: fully unrolled dot products), 0 for any
+template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* __restrict__ qkv,
                                                                   const __half* __restrict__ bias,
                                                                   const float* __restrict__ inv_freq,
                                                                   const int64_t* __restrict__ pos_p, __half* kc,
                                                                   __half* vc, float* __restrict__ part_o,
-                                                                  float* __restrict__ part_ml, int nh, int nkv, int hd,
-                                                                  int max_len, float scale) {
+                                                                  float* __restrict__ part_ml, int nh, int nkv, int hd_,
+                                                                  int max_len_, float scale) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
   pdl_launch_dependents();
+  const int hd = HD ? HD : hd_, max_len = max_len_;
   const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
   const int g = nh / nkv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32, half = hd / 2;
   const int ks = attn_k_stride(hd);
@@ -154,38 +157,59 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
   }
   cp_async_commit();
   pdl_wait();   // qkv comes from the previous kernel in the stream
-  // q of the group's heads, and (in the range holding pos) this token's k and v
+  // q of the group's heads, and (in the range holding pos) this token's k and v: thread (row, quad) takes dims
+  // j..j+3 and their rotate-half partners j+hd/2..j+hd/2+3 with 8-byte loads, all issued in one round
   const bool mine = pos < p0 + kAttnChunk;
-  for (int i = threadIdx.x; i < (g + (mine ? 2 : 0)) * half; i += blockDim.x) {
-    const int hh = i / half, j = i - hh * half;
+  const int quads = half / 4;
+  for (int i = threadIdx.x; i < (g + (mine ? 2 : 0)) * quads; i += blockDim.x) {
+    const int hh = i / quads, j = (i - hh * quads) * 4;
     const int head = hh < g ? kvh * g + hh : hh == g ? nh + kvh : nh + nkv + kvh;   // q / k / v row of qkv
     const __half* src = qkv + (size_t)head * hd;
-    float a = __half2float(src[j]), b = __half2float(src[j + half]);
+    uint2 ua = *reinterpret_cast<const uint2*>(src + j), ub = *reinterpret_cast<const uint2*>(src + j + half);
     if (bias) {
-      a = __half2float(__hadd(src[j], bias[(size_t)head * hd + j]));
-      b = __half2float(__hadd(src[j + half], bias[(size_t)head * hd + j + half]));
+      const uint2 ba = *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j);
+      const uint2 bb = *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j + half);
+      __half2* pa = reinterpret_cast<__half2*>(&ua);
+      __half2* pb = reinterpret_cast<__half2*>(&ub);
+      pa[0] = __hadd2(pa[0], *reinterpret_cast<const __half2*>(&ba.x));
+      pa[1] = __hadd2(pa[1], *reinterpret_cast<const __half2*>(&ba.y));
+      pb[0] = __hadd2(pb[0], *reinterpret_cast<const __half2*>(&bb.x));
+      pb[1] = __hadd2(pb[1], *reinterpret_cast<const __half2*>(&bb.y));
     }
+    const __half* ha4 = reinterpret_cast<const __half*>(&ua);
+    const __half* hb4 = reinterpret_cast<const __half*>(&ub);
     if (hh == g + 1) {   // v: no rotation
-      const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-      sv[(pos - p0) * hd + j] = ha;
-      sv[(pos - p0) * hd + j + half] = hb;
-      vc[((size_t)kvh * max_len + pos) * hd + j] = ha;
-      vc[((size_t)kvh * max_len + pos) * hd + j + half] = hb;
+      *reinterpret_cast<uint2*>(sv + (pos - p0) * hd + j) = ua;
+      *reinterpret_cast<uint2*>(sv + (pos - p0) * hd + j + half) = ub;
+      *reinterpret_cast<uint2*>(vc + ((size_t)kvh * max_len + pos) * hd + j) = ua;
+      *reinterpret_cast<uint2*>(vc + ((size_t)kvh * max_len + pos) * hd + j + half) = ub;
       continue;
     }
-    float sn, cs;
-    sincosf((float)pos * inv_freq[j], &sn, &cs);
-    float ra, rb;
-    rope_pair(a, b, cs, sn, ra, rb);
-    const __half ha = __float2half_rn(ra), hb = __float2half_rn(rb);
+    const float4 fr = *reinterpret_cast<const float4*>(inv_freq + j);
+    const float frq[4] = {fr.x, fr.y, fr.z, fr.w};
+    __half ra4[4], rb4[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float sn, cs;
+      sincosf((float)pos * frq[c], &sn, &cs);
+      float ra, rb;
+      rope_pair(__half2float(ha4[c]), __half2float(hb4[c]), cs, sn, ra, rb);
+      ra4[c] = __float2half_rn(ra);
+      rb4[c] = __float2half_rn(rb);
+    }
     if (hh < g) {   // q rounded to fp16 like the reference path, then scaled in fp32
-      sq[hh * hd + j] = __half2float(ha) * scale;
-      sq[hh * hd + j + half] = __half2float(hb) * scale;
+      *reinterpret_cast<float4*>(sq + hh * hd + j) =
+          make_float4(__half2float(ra4[0]) * scale, __half2float(ra4[1]) * scale, __half2float(ra4[2]) * scale,
+                      __half2float(ra4[3]) * scale);
+      *reinterpret_cast<float4*>(sq + hh * hd + j + half) =
+          make_float4(__half2float(rb4[0]) * scale, __half2float(rb4[1]) * scale, __half2float(rb4[2]) * scale,
+                      __half2float(rb4[3]) * scale);
     } else {
-      sk[(pos - p0) * ks + j] = ha;
-      sk[(pos - p0) * ks + j + half] = hb;
-      kc[((size_t)kvh * max_len + pos) * hd + j] = ha;
-      kc[((size_t)kvh * max_len + pos) * hd + j + half] = hb;
+      const uint2 ka = *reinterpret_cast<const uint2*>(ra4), kb = *reinterpret_cast<const uint2*>(rb4);
+      *reinterpret_cast<uint2*>(sk + (pos - p0) * ks + j) = ka;
+      *reinterpret_cast<uint2*>(sk + (pos - p0) * ks + j + half) = kb;
+      *reinterpret_cast<uint2*>(kc + ((size_t)kvh * max_len + pos) * hd + j) = ka;
+      *reinterpret_cast<uint2*>(kc + ((size_t)kvh * max_len + pos) * hd + j + half) = kb;
     }
   }
   cp_async_wait<0>();
@@ -197,7 +221,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       const float* q = sq + h * hd;
       const __half* k = sk + p * ks;
       float d0 = 0.f, d1 = 0.f;
-      for (int e = 0; e < hd; e += 8) {
+#pragma unroll
+      for (int e = 0; e < (HD ? HD : hd); e += 8) {
         const uint4 kr = *reinterpret_cast<const uint4*>(k + e);
         const float4 qa = *reinterpret_cast<const float4*>(q + e);
         const float4 qb = *reinterpret_cast<const float4*>(q + e + 4);
@@ -241,6 +266,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
   for (int i = threadIdx.x; i < g * q4; i += blockDim.x) {
     const int h = i / q4, e0 = (i - h * q4) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
     for (int p = 0; p < np; ++p) {
       const float w = ss[h * kAttnChunk + p];
       const uint2 vr = *reinterpret_cast<const uint2*>(sv + p * hd + e0);
@@ -255,18 +281,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
   }
 }
 
-// out[head] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s; grid nh, block hd. The splits' (m, l) pairs are
-// read once into shared memory (in parallel), warp 0 turns them into weights exp(m_s - M) (0 for empty splits)
-// and their weighted sum, and the hd-long partial rows are read with independent loads.
+// out[head] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s over the splits that hold rows 0..pos (the others
+// are empty); grid nh, block hd. The splits' (m, l) pairs are read once into shared memory (in parallel), warp 0
+// turns them into weights exp(m_s - M) and their weighted sum, and the hd-long partial rows are read with
+// independent loads.
 constexpr int kCombineMaxSplits = 1024;
-__global__ void attn_combine_kernel(const float* part_o, const float* part_ml, __half* out, int nh, int nkv, int hd,
-                                    int nsplit) {
+__global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const int64_t* __restrict__ pos_p,
+                                    __half* out, int nh, int nkv, int hd, int nsplit, int max_len) {
   __shared__ float sw[kCombineMaxSplits], sl[kCombineMaxSplits];
   __shared__ float s_den;
   pdl_launch_dependents();
+  const int64_t pos = *pos_p;
   pdl_wait();
+  if (pos < 0 || pos >= max_len) return;   // the split kernel has recorded the bad position
+  const int nact = min(nsplit, (int)(pos / kAttnChunk) + 1);
   const int head = blockIdx.x, e = threadIdx.x, g = nh / nkv, kvh = head / g, h = head - kvh * g;
-  for (int s = threadIdx.x; s < nsplit; s += blockDim.x) {
+  for (int s = threadIdx.x; s < nact; s += blockDim.x) {
     const float2 v = *reinterpret_cast<const float2*>(part_ml + (((size_t)kvh * nsplit + s) * g + h) * 2);
     sw[s] = v.x;
     sl[s] = v.y;
@@ -275,13 +305,12 @@ __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, _
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float M = -INFINITY;
-    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, sw[s]);
+    for (int s = lane; s < nact; s += 32) M = fmaxf(M, sw[s]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float den = 0.f;
-    for (int s = lane; s < nsplit; s += 32) {
-      const float m = sw[s];
-      const float w = m == -INFINITY ? 0.f : expf(m - M);
+    for (int s = lane; s < nact; s += 32) {
+      const float w = expf(sw[s] - M);
       sw[s] = w;
       den += w * sl[s];
     }
@@ -290,11 +319,9 @@ __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, _
   }
   __syncthreads();
   float num = 0.f;
-#pragma unroll 4
-  for (int s = 0; s < nsplit; ++s) {
-    const float w = sw[s];
-    if (w != 0.f) num += w * part_o[(((size_t)kvh * nsplit + s) * g + h) * hd + e];
-  }
+  const float* po = part_o + ((size_t)kvh * nsplit * g + h) * hd + e;
+#pragma unroll 8
+  for (int s = 0; s < nact; ++s) num += sw[s] * po[(size_t)s * g * hd];
   out[(size_t)head * hd + e] = __float2half_rn(num / s_den);
 }
 
@@ -366,13 +393,14 @@ cudaError_t launch_attention(const __half* qkv, const __half* bias, const float*
                              int hd, int max_len, cudaStream_t st) {
   const int nsplit = attn_splits(max_len);
   const size_t smem = attn_smem_bytes(nh, nkv, hd);
-  cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kern = hd == 128 ? attn_split_kernel<128> : hd == 64 ? attn_split_kernel<64> : attn_split_kernel<0>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(attn_split_kernel, dim3(nkv, nsplit), dim3(kAttnThreads), smem, st, qkv, bias, inv_freq, pos, kc, vc,
-                 part_o, part_ml, nh, nkv, hd, max_len, 1.f / sqrtf((float)hd));
+  e = launch_pdl(kern, dim3(nkv, nsplit), dim3(kAttnThreads), smem, st, qkv, bias, inv_freq, pos, kc, vc, part_o,
+                 part_ml, nh, nkv, hd, max_len, 1.f / sqrtf((float)hd));
   if (e != cudaSuccess) return e;
-  return launch_pdl(attn_combine_kernel, dim3(nh), dim3(hd), 0, st, (const float*)part_o, (const float*)part_ml, out, nh,
-                    nkv, hd, nsplit);
+  return launch_pdl(attn_combine_kernel, dim3(nh), dim3(hd), 0, st, (const float*)part_o, (const float*)part_ml, pos,
+                    out, nh, nkv, hd, nsplit, max_len);
 }
 
 // Scratch of lb_decode_attention_noalloc: the split partials (part_o, then part_ml) of callers that cannot pass
