@@ -127,7 +127,8 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  *
  * lb_decode_embed:     x[H] = emb[*tok][:]                       (tok: int64 on the device)
  * lb_decode_rmsnorm:   if r: x = x + r; h = w * fp16(x * rsqrt(mean(x^2) + eps))   (Qwen2RMSNorm); H % 8 == 0,
- *                      all four arrays 16-byte aligned (r may be NULL)
+ *                      all four arrays 16-byte aligned (r may be NULL); w (model state) is read before the kernel
+ *                      waits on the previous kernel in the stream
  * lb_decode_attention: qkv = [q (nh x hd) | k (nkv x hd) | v (nkv x hd)] of the fused projection, + bias (may be
  *                      NULL); q and k rotated by the rotate-half RoPE at angle pos * inv_freq[j] (fp32 [hd/2]);
  *                      k, v appended to the caches [nkv, max_len, hd] at row pos; then one query token attends
@@ -135,8 +136,8 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  *                      part_o (fp32, nh * lb_decode_attention_splits(max_len) * hd) and part_ml (fp32, twice
  *                      nh * splits) are caller-owned scratch; qkv, bias, inv_freq, the caches and part_o 16-byte
  *                      aligned, part_ml 8-byte aligned; hd a multiple of
- *                      8 (<= 1024), max_len <= 65536; the cache rows below pos are read before the kernel waits on
- *                      the previous kernel in the stream (they must not be its output); a pos outside
+ *                      8 (<= 1024), max_len <= 65536; the cache rows below pos, bias and inv_freq are read before the
+ *                      kernel waits on the previous kernel in the stream (they must not be its output); a pos outside
  *                      0..max_len-1 writes nothing and sets lb_device_error() to 3
  * lb_decode_silu_mul:  a[I] = fp16(silu(gu[i])) * gu[I + i]     (gu = [gate | up])
  */

@@ -36,15 +36,19 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(__half* __restrict
                                                               int H, float eps) {
   __shared__ float red[32];
   pdl_launch_dependents();
-  pdl_wait();
   const int n8 = H / 8;
   uint4 xv[kRmsVec], rv[kRmsVec], wv[kRmsVec];
+#pragma unroll
+  for (int j = 0; j < kRmsVec; ++j) {   // the norm weights are model state: fetched before the dependency wait
+    const int i = threadIdx.x + j * kRmsThreads;
+    if (i < n8) wv[j] = reinterpret_cast<const uint4*>(w)[i];
+  }
+  pdl_wait();
 #pragma unroll
   for (int j = 0; j < kRmsVec; ++j) {
     const int i = threadIdx.x + j * kRmsThreads;
     if (i < n8) {
       xv[j] = reinterpret_cast<const uint4*>(x)[i];
-      wv[j] = reinterpret_cast<const uint4*>(w)[i];
       if (r) rv[j] = reinterpret_cast<const uint4*>(r)[i];
     }
   }
@@ -156,19 +160,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     cp_async16(smem_addr(sv + r * hd + c8), vg + (size_t)r * hd + c8);
   }
   cp_async_commit();
-  pdl_wait();   // qkv comes from the previous kernel in the stream
   // q of the group's heads, and (in the range holding pos) this token's k and v: thread (row, quad) takes dims
-  // j..j+3 and their rotate-half partners j+hd/2..j+hd/2+3 with 8-byte loads, all issued in one round
+  // j..j+3 and their rotate-half partners j+hd/2..j+hd/2+3 with 8-byte loads, all issued in one round; the bias
+  // and frequencies of the thread's first item are model state, fetched before the dependency wait
   const bool mine = pos < p0 + kAttnChunk;
-  const int quads = half / 4;
-  for (int i = threadIdx.x; i < (g + (mine ? 2 : 0)) * quads; i += blockDim.x) {
+  const int quads = half / 4, items = (g + (mine ? 2 : 0)) * quads;
+  auto item_head = [&](int hh) { return hh < g ? kvh * g + hh : hh == g ? nh + kvh : nh + nkv + kvh; };
+  uint2 ba0 = make_uint2(0, 0), bb0 = make_uint2(0, 0);
+  float4 fr0 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (threadIdx.x < items) {
+    const int hh = threadIdx.x / quads, j = (threadIdx.x - hh * quads) * 4;
+    if (bias) {
+      ba0 = *reinterpret_cast<const uint2*>(bias + (size_t)item_head(hh) * hd + j);
+      bb0 = *reinterpret_cast<const uint2*>(bias + (size_t)item_head(hh) * hd + j + half);
+    }
+    fr0 = *reinterpret_cast<const float4*>(inv_freq + j);
+  }
+  pdl_wait();   // qkv comes from the previous kernel in the stream
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
     const int hh = i / quads, j = (i - hh * quads) * 4;
-    const int head = hh < g ? kvh * g + hh : hh == g ? nh + kvh : nh + nkv + kvh;   // q / k / v row of qkv
+    const int head = item_head(hh);   // q / k / v row of qkv
     const __half* src = qkv + (size_t)head * hd;
     uint2 ua = *reinterpret_cast<const uint2*>(src + j), ub = *reinterpret_cast<const uint2*>(src + j + half);
+    const bool first = i == threadIdx.x;
     if (bias) {
-      const uint2 ba = *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j);
-      const uint2 bb = *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j + half);
+      const uint2 ba = first ? ba0 : *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j);
+      const uint2 bb = first ? bb0 : *reinterpret_cast<const uint2*>(bias + (size_t)head * hd + j + half);
       __half2* pa = reinterpret_cast<__half2*>(&ua);
       __half2* pb = reinterpret_cast<__half2*>(&ub);
       pa[0] = __hadd2(pa[0], *reinterpret_cast<const __half2*>(&ba.x));
@@ -185,7 +202,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       *reinterpret_cast<uint2*>(vc + ((size_t)kvh * max_len + pos) * hd + j + half) = ub;
       continue;
     }
-    const float4 fr = *reinterpret_cast<const float4*>(inv_freq + j);
+    const float4 fr = first ? fr0 : *reinterpret_cast<const float4*>(inv_freq + j);
     const float frq[4] = {fr.x, fr.y, fr.z, fr.w};
     __half ra4[4], rb4[4];
 #pragma unroll

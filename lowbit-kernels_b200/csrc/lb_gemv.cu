@@ -554,17 +554,23 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     return v;
   };
   if constexpr (EPI == 1) {
-    // SwiGLU over interleaved rows (M = 1): element (i, lane) of row tile r holds row 16 r + q with q = lane / 4
-    // (i = 0) or 8 + lane / 4 (i = 2); thread j < 8 RT combines rows 2j (gate) and 2j + 1 (up) of the CTA's rows
-    // into output n0 / 2 + j, with the roundings of the separate GEMV and SiLU*up kernels
+    // SwiGLU over interleaved rows (M = 1): the CTA's 16 RT row sums are formed in parallel (element (i, lane) of
+    // row tile r holds row 16 r + lane / 4 for i = 0 and 16 r + 8 + lane / 4 for i = 2) and rounded to fp16 like
+    // the GEMV's output; thread j < 8 RT then combines rows 2j (gate) and 2j + 1 (up) into output n0 / 2 + j, with
+    // the roundings of the separate SiLU*up kernel
+    __shared__ float rows_f[16 * RT];
+    for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
+      const int rm = e >> 7, i = (e >> 5) & 3, ln = e & 31;
+      const int r = rm / MT, mt = rm - r * MT;
+      if (mt == 0 && (ln & 3) == 0 && (i & 1) == 0)
+        rows_f[16 * r + (ln >> 2) + (i >= 2 ? 8 : 0)] = __half2float(__float2half_rn(tile_sum(e)));
+    }
+    __syncthreads();
     if (threadIdx.x < 8 * RT) {
-      const int j = threadIdx.x, r = j >> 3, rg = 2 * (j & 7), ru = rg + 1;
-      const int base = r * MT * 128;
-      const float gv = tile_sum(base + (rg < 8 ? 0 : 64) + 4 * (rg & 7));
-      const float uv = tile_sum(base + (ru < 8 ? 0 : 64) + 4 * (ru & 7));
-      const float gf = __half2float(__float2half_rn(gv));
+      const int j = threadIdx.x;
+      const float gf = rows_f[2 * j], uf = rows_f[2 * j + 1];
       const __half sg = __float2half_rn(gf / (1.f + expf(-gf)));
-      if (n0 + 16 * r + ru < N) p.y[n0 / 2 + j] = __float2half_rn(__half2float(sg) * __half2float(__float2half_rn(uv)));
+      if (n0 + 2 * j + 1 < N) p.y[n0 / 2 + j] = __float2half_rn(__half2float(sg) * uf);
     }
     return;
   }
