@@ -119,7 +119,7 @@ def _rope(t, pos, inv_freq):
 
 
 @pytest.mark.parametrize("pos", [0, 63, 64, 257, 3000])
-@pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64)])
+@pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64), (8, 2, 96)])   # 96: the generic path
 def test_fused_attention_kernel(pos, heads):
     nh, nkv, hd = heads
     max_len = 320 if pos < 320 else 4096     # 3000: 47 splits hold cached rows, 17 are empty
