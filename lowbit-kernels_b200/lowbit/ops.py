@@ -81,6 +81,24 @@ class W4Weight:
         """Bytes of one copy of the weight (packed values + scales), whatever layouts are kept."""
         return self.n * self.k // 2 + self.scales.numel() * 2
 
+    def launch_args(self, version):
+        """(packed pointer, scales pointer, device index) of the layout `version` reads, or None if that layout is
+        not kept or not launchable; validated once per tensor object (replacing a layout tensor revalidates)."""
+        w, s = getattr(self, NEEDS[version]), self.scales
+        cache = self.__dict__.setdefault("_launch", {})
+        hit = cache.get(version)
+        if hit is not None and hit[0] is w and hit[1] is s:
+            return hit[2]
+        args = None
+        if (w is not None and w.is_cuda and s.is_cuda and w.device == s.device and w.dtype == torch.uint8
+                and s.dtype == torch.float16 and w.is_contiguous() and s.is_contiguous() and w.dim() == 2
+                and s.dim() == 2 and tuple(w.shape) == (self.n, self.k // 2) and self.group > 0
+                and self.group % 32 == 0 and self.k % self.group == 0
+                and tuple(s.shape) == (self.n, self.k // self.group)):
+            args = (w.data_ptr(), s.data_ptr(), w.get_device())
+        cache[version] = (w, s, args)
+        return args
+
 
 def pick_rows(n, m):
     """Rows per warp the compatibility kernels (versions 1-4) use when rows_per_warp = 0 (csrc/w4_gemv.cu:424-427)."""
@@ -92,10 +110,52 @@ NEEDS = {1: "packed", 2: "packed", 3: "packed_v3", 4: "packed_v3", 5: "packed_mm
 MAX_ROWS = {1: 8, 2: 8, 3: 8, 4: 8, 5: 64, 6: 8}
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream(dev):
+    return _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream(dev).cuda_stream
+
+
+def _gemv_fast(x, wq, version, out):
+    """The common decode call with the weight's validated launch arguments cached: cheap checks on x and out, one
+    C call. None when anything is unusual -- the checked path below then handles it (and raises its errors)."""
+    args = wq.launch_args(version)
+    if args is None:
+        return None
+    w_ptr, s_ptr, dev = args
+    if (type(x) is not torch.Tensor or x.dtype != torch.float16 or x.dim() != 2 or x.shape[1] != wq.k
+            or x.shape[0] == 0 or x.get_device() != dev or not x.is_contiguous()
+            or torch.cuda.current_device() != dev):
+        return None
+    m, n = x.shape[0], wq.n
+    if out is None:
+        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+    elif (out.dtype == torch.float16 and out.dim() == 2 and out.shape[0] == m and out.shape[1] == n
+          and out.get_device() == dev and out.is_contiguous()):
+        y = out
+    else:
+        return None
+    e = ext()
+    if version == 6:
+        rc = e.lib.lb_w4_gemv(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, wq.k, wq.group, 6, 0,
+                              _current_stream(dev))
+    else:
+        rc = e.lib.lb_w4_gemm_tc(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, wq.k, wq.group, 0,
+                                 _current_stream(dev))
+    if rc:
+        e._raise(rc)
+    return y
+
+
 def gemv(x, wq, version=4, rows_per_warp=0, out=None):
     """x [M, K] fp16 -> [M, N] fp16. Versions 1-4 and 6: M <= 8; version 5: M <= 64 (tensor cores).
     Versions 5 and 6 read the same layout (packed_mma), so a model needs only that copy. `out`: an optional
     contiguous fp16 [M, N] tensor the result is written into (no allocation)."""
+    if (version == 5 or version == 6) and rows_per_warp == 0 and isinstance(wq, W4Weight):
+        y = _gemv_fast(x, wq, version, out)
+        if y is not None:
+            return y
     if version not in NEEDS:
         raise ValueError(f"version must be one of {sorted(NEEDS)}")
     if getattr(wq, NEEDS[version]) is None:

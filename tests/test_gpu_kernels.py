@@ -298,6 +298,30 @@ def test_linear_out_writes_in_place_with_the_same_bits():
         ops.linear(torch.randn(1, 1536).half().cuda(), wq, out=torch.empty(1, 999, device="cuda").half())
 
 
+def test_cached_launch_path_matches_the_checked_path():
+    """ops.gemv's cached-argument path (versions 5 and 6) gives the bits of the fully checked call; unusual inputs
+    (a strided x) take the checked path; replacing a layout tensor revalidates the cache."""
+    e = ops.ext()
+    wq = ops.W4Weight.from_float(torch.randn(2048, 1536))
+    for m, v in ((1, 6), (4, 6), (24, 5)):
+        x = torch.randn(m, 1536).half().cuda()
+        if v == 6:
+            want = e.w4_gemv(x, wq.packed_mma, wq.scales, wq.group, 6)
+        else:
+            want = e.w4_gemm_tc(x, wq.packed_mma, wq.scales, wq.group)
+        assert torch.equal(ops.gemv(x, wq, v), want)
+        assert v in wq._launch and wq._launch[v][2] is not None
+        out = torch.empty(m, 2048, device="cuda").half()
+        assert ops.gemv(x, wq, v, out=out) is out and torch.equal(out, want)
+    xs = torch.randn(1536, 2).half().cuda().t()[:1]            # not contiguous
+    assert torch.equal(ops.gemv(xs, wq, 6), e.w4_gemv(xs.contiguous(), wq.packed_mma, wq.scales, wq.group, 6))
+    x = torch.randn(1, 1536).half().cuda()
+    before = ops.gemv(x, wq, 6)
+    wq.packed_mma = wq.packed_mma.clone()
+    assert torch.equal(ops.gemv(x, wq, 6), before)
+    assert wq._launch[6][0] is wq.packed_mma
+
+
 def test_fixed_version_past_its_limit_falls_back():
     wq = ops.W4Weight.from_float(torch.randn(256, 512))
     x = torch.randn(9, 512).half().cuda()
