@@ -148,16 +148,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     return;
   }
   __half* sk = reinterpret_cast<__half*>(sm_raw);               // [64][ks]
-  __half* sv = sk + kAttnChunk * ks;                             // [64][hd]
-  float* sq = reinterpret_cast<float*>(sv + kAttnChunk * hd);    // [g][hd]
+  __half* sv = sk + kAttnChunk * ks;                             // [64][ks]
+  float* sq = reinterpret_cast<float*>(sv + kAttnChunk * ks);    // [g][hd]
   float* ss = sq + g * hd;                                       // [g][64]
+  __half* q16 = reinterpret_cast<__half*>(ss + g * kAttnChunk);  // [8][ks]   tensor-core path: q in fp16
+  __half* p16 = q16 + 8 * ks;                                    // [8][72]   tensor-core path: exp(s - m) in fp16
+  // scores and P V on the tensor cores (mma.sync m16n8k16, the group's heads as the 8 columns) when the group
+  // fits one n-tile and the head dim is a compile-time 64 or 128; the scalar loops otherwise
+  const bool use_mma = HD != 0 && g <= 8;
   const int ncached = min(np, pos - p0), vec = hd / 8;
   const __half* kg = kc + ((size_t)kvh * max_len + p0) * hd;
   const __half* vg = vc + ((size_t)kvh * max_len + p0) * hd;
   for (int i = threadIdx.x; i < ncached * vec; i += blockDim.x) {
     const int r = i / vec, c8 = (i - r * vec) * 8;
     cp_async16(smem_addr(sk + r * ks + c8), kg + (size_t)r * hd + c8);
-    cp_async16(smem_addr(sv + r * hd + c8), vg + (size_t)r * hd + c8);
+    cp_async16(smem_addr(sv + r * ks + c8), vg + (size_t)r * hd + c8);
   }
   cp_async_commit();
   // q of the group's heads, and (in the range holding pos) this token's k and v: thread (row, quad) takes dims
@@ -196,8 +201,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     const __half* ha4 = reinterpret_cast<const __half*>(&ua);
     const __half* hb4 = reinterpret_cast<const __half*>(&ub);
     if (hh == g + 1) {   // v: no rotation
-      *reinterpret_cast<uint2*>(sv + (pos - p0) * hd + j) = ua;
-      *reinterpret_cast<uint2*>(sv + (pos - p0) * hd + j + half) = ub;
+      *reinterpret_cast<uint2*>(sv + (pos - p0) * ks + j) = ua;
+      *reinterpret_cast<uint2*>(sv + (pos - p0) * ks + j + half) = ub;
       *reinterpret_cast<uint2*>(vc + ((size_t)kvh * max_len + pos) * hd + j) = ua;
       *reinterpret_cast<uint2*>(vc + ((size_t)kvh * max_len + pos) * hd + j + half) = ub;
       continue;
@@ -215,6 +220,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       rb4[c] = __float2half_rn(rb);
     }
     if (hh < g) {   // q rounded to fp16 like the reference path, then scaled in fp32
+      *reinterpret_cast<uint2*>(q16 + hh * ks + j) = *reinterpret_cast<const uint2*>(ra4);
+      *reinterpret_cast<uint2*>(q16 + hh * ks + j + half) = *reinterpret_cast<const uint2*>(rb4);
       *reinterpret_cast<float4*>(sq + hh * hd + j) =
           make_float4(__half2float(ra4[0]) * scale, __half2float(ra4[1]) * scale, __half2float(ra4[2]) * scale,
                       __half2float(ra4[3]) * scale);
@@ -229,8 +236,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       *reinterpret_cast<uint2*>(kc + ((size_t)kvh * max_len + pos) * hd + j + half) = kb;
     }
   }
+  if (use_mma) {   // V rows past the range enter the P V products (times P = 0): make them finite
+    for (int i = threadIdx.x; i < (kAttnChunk - np) * (hd / 8); i += blockDim.x) {
+      const int r = np + i / (hd / 8), c8 = (i % (hd / 8)) * 8;
+      *reinterpret_cast<uint4*>(sv + r * ks + c8) = make_uint4(0, 0, 0, 0);
+    }
+  }
   cp_async_wait<0>();
   __syncthreads();
+  if (use_mma) {
+    // S^T[16 positions][8 heads] per warp 0..3: A = K rows (ldmatrix), B = q16 rows; scaled in fp32 afterwards
+    if (warp < 4 && warp * 16 < np) {
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t a_base =
+          smem_addr(sk + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ks + (lane >> 4) * 8);
+      const uint32_t b_base = smem_addr(q16 + (lane & 7) * ks + ((lane >> 3) & 1) * 8);
+#pragma unroll
+      for (int kk = 0; kk < (HD ? HD : 16) / 16; ++kk) {
+        uint32_t a[4], b[2];
+        ldsm_x4(a, a_base + kk * 32);
+        ldsm_x2(b, b_base + kk * 32);
+        mma16816(dd, a[0], a[1], a[2], a[3], b[0], b[1]);
+      }
+      const int gq = lane >> 2, tq = lane & 3;
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int p = warp * 16 + gq + 8 * r, h = 2 * tq + c;
+          if (p < np && h < g) ss[h * kAttnChunk + p] = dd[2 * r + c] * scale;
+        }
+    }
+  } else {
   // scores: thread (head h, position p), the whole dot product in fp32
   for (int i = threadIdx.x; i < g * kAttnChunk; i += blockDim.x) {
     const int h = i / kAttnChunk, p = i - h * kAttnChunk;
@@ -258,6 +295,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       ss[h * kAttnChunk + p] = d0 + d1;
     }
   }
+  }
   __syncthreads();
   // per head: max and exponentials (warp h handles heads h, h + nw, ...)
   for (int h = warp; h < g; h += nw) {
@@ -266,10 +304,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
-    for (int p = lane; p < np; p += 32) {
-      const float e = expf(ss[h * kAttnChunk + p] - m);
-      ss[h * kAttnChunk + p] = e;
-      l += e;
+    if (use_mma) {   // P in fp16 (zero past the range), and l summed from the rounded values P V uses
+      for (int p = lane; p < kAttnChunk; p += 32) {
+        const __half e = __float2half_rn(p < np ? expf(ss[h * kAttnChunk + p] - m) : 0.f);
+        p16[h * 72 + p] = e;
+        l += __half2float(e);
+      }
+    } else {
+      for (int p = lane; p < np; p += 32) {
+        const float e = expf(ss[h * kAttnChunk + p] - m);
+        ss[h * kAttnChunk + p] = e;
+        l += e;
+      }
     }
     l = warp_sum(l);
     if (lane == 0) {
@@ -278,6 +324,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
     }
   }
   __syncthreads();
+  if (use_mma) {
+    // O^T[16 dims][8 heads] per warp: A = V^T (ldmatrix.trans of V rows), B = P rows; 16 positions per step
+    if (warp < (HD ? HD : 16) / 16) {
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+      const int jm = lane >> 3, rm = lane & 7;
+      const uint32_t a_base = smem_addr(sv + (rm + (jm >= 2 ? 8 : 0)) * ks + warp * 16 + (jm & 1) * 8);
+      const uint32_t b_base = smem_addr(p16 + (lane & 7) * 72 + ((lane >> 3) & 1) * 8);
+#pragma unroll
+      for (int kb = 0; kb < kAttnChunk / 16; ++kb) {
+        if (kb * 16 >= np) break;
+        uint32_t a[4], b[2];
+        ldsm_x4_trans(a, a_base + kb * 16 * ks * 2);
+        ldsm_x2(b, b_base + kb * 32);
+        mma16816(dd, a[0], a[1], a[2], a[3], b[0], b[1]);
+      }
+      const int gq = lane >> 2, tq = lane & 3;
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int e = warp * 16 + gq + 8 * r, h = 2 * tq + c;
+          if (h < g) part_o[(pbase + h) * hd + e] = dd[2 * r + c];
+        }
+    }
+    return;
+  }
   // unnormalized outputs: thread (h, 4 dims) sums over the range's positions
   const int q4 = hd / 4;
   for (int i = threadIdx.x; i < g * q4; i += blockDim.x) {
@@ -286,7 +358,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
 #pragma unroll 8
     for (int p = 0; p < np; ++p) {
       const float w = ss[h * kAttnChunk + p];
-      const uint2 vr = *reinterpret_cast<const uint2*>(sv + p * hd + e0);
+      const uint2 vr = *reinterpret_cast<const uint2*>(sv + p * ks + e0);
       const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
       const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
       acc.x += w * v01.x;
@@ -400,8 +472,8 @@ void decode_clear_device_error() {
 }
 
 size_t attn_smem_bytes(int nh, int nkv, int hd) {
-  const int g = nh / nkv;
-  return (size_t)kAttnChunk * (attn_k_stride(hd) + hd) * sizeof(__half) +
+  const int g = nh / nkv, ks = attn_k_stride(hd);
+  return (size_t)(2 * kAttnChunk * ks + 8 * ks + 8 * 72) * sizeof(__half) +
          (size_t)(g * hd + g * kAttnChunk) * sizeof(float);
 }
 
