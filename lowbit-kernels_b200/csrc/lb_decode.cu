@@ -220,8 +220,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __half* 
       rb4[c] = __float2half_rn(rb);
     }
     if (hh < g) {   // q rounded to fp16 like the reference path, then scaled in fp32
-      *reinterpret_cast<uint2*>(q16 + hh * ks + j) = *reinterpret_cast<const uint2*>(ra4);
-      *reinterpret_cast<uint2*>(q16 + hh * ks + j + half) = *reinterpret_cast<const uint2*>(rb4);
+      if (use_mma) {   // q16 holds 8 rows: only groups of up to 8 heads take the tensor-core path
+        *reinterpret_cast<uint2*>(q16 + hh * ks + j) = *reinterpret_cast<const uint2*>(ra4);
+        *reinterpret_cast<uint2*>(q16 + hh * ks + j + half) = *reinterpret_cast<const uint2*>(rb4);
+      }
       *reinterpret_cast<float4*>(sq + hh * hd + j) =
           make_float4(__half2float(ra4[0]) * scale, __half2float(ra4[1]) * scale, __half2float(ra4[2]) * scale,
                       __half2float(ra4[3]) * scale);

@@ -119,7 +119,9 @@ def _rope(t, pos, inv_freq):
 
 
 @pytest.mark.parametrize("pos", [0, 63, 64, 257, 3000])
-@pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64), (8, 2, 96)])   # 96: the generic path
+# (16, 2, 128), (28, 4, 128), (4, 2, 64): tensor-core scores and P V; (32, 2, 128): 16 heads per kv head, the
+# scalar loops at a compile-time head dim; (8, 2, 96): the generic path
+@pytest.mark.parametrize("heads", [(16, 2, 128), (28, 4, 128), (4, 2, 64), (32, 2, 128), (8, 2, 96)])
 def test_fused_attention_kernel(pos, heads):
     nh, nkv, hd = heads
     max_len = 320 if pos < 320 else 4096     # 3000: 47 splits hold cached rows, 17 are empty
