@@ -1,6 +1,7 @@
 """Benchmark: W4A16 GEMV HBM throughput on the Qwen2.5 decode projections, B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-per-shape] [--no-cpu]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-per-shape] [--no-skinny]
+                    [--no-dequant] [--no-decode] [--no-cpu]
 
 A step is one decode pass (M = 1) over every projection of Qwen2.5-0.5B, 1.5B and 3B: q, k, v, o, gate, up,
 down -- 21 GEMV calls. Weights are cold: the step cycles through enough distinct copies of the 21 weights
@@ -17,6 +18,17 @@ by time.
   cpu_baseline / --impl reference
           the reference's CPU path (dequantize on CPU tensors + fp32 F.linear, lowbit/ops.py:119-123) restated in
           oracle/oracle.py, timed on the host cores of this machine.
+
+The same line carries the other BASELINE configurations, measured after the timed sweep in the same run:
+  per_shape   each config-1 projection alone (cold copies), with the reference's own gemv_v6 on the same copies
+              (ref_us; the reference's csrc/w4_gemv.cu built unchanged for sm_100a into oracle/_ref/);
+  skinny      config 2: M = 2..64 over the config-1 and tail shapes -- the kernel linear() picks, the INT4
+              tensor-core kernel, dequantize + cuBLAS and fp16 cuBLAS in the same run, and the reference's gemm_v5;
+  dequant     north-star subsystem 3: the prefill dequantize kernel per shape, and dequantize + cuBLAS against
+              fp16 cuBLAS at 128-1024 rows;
+  decode_3b   config 3: Qwen2.5-3B batch-1 decode tok/s, one CUDA graph per step (replicas at N > 1);
+  tp_decode   config 4: Qwen2.5-7B tensor-parallel decode tok/s over all ranks (the unsharded model at N = 1).
+The kernel legs run at N = 1 only; the decoder legs at every N.
 
 Under torchrun (--gpus N > 1) each rank runs the same sweep on its own GPU (the single-layer benchmark has no
 exchange step: replicas, weak scaling); value sums all ranks' bytes over the slowest rank's time.
@@ -37,8 +49,12 @@ for p in (ROOT / "lowbit-kernels_b200", ROOT):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
+import faulthandler  # noqa: E402
+
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
+
+faulthandler.enable()   # a crash in native code prints the Python stack
 
 METRIC = "W4A16 GEMV HBM GB/s (% of ~8 TB/s) at M=1-64; Qwen2.5-3B decode tok/s"
 MODELS = {  # hidden, intermediate, q width, kv width
@@ -79,18 +95,15 @@ def measured_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes (read + write) per launch of the GEMV over one sweep step, from the committed ncu summary
-    (profiles/gemv_oneshot_m1_sweep_dram.md), or None when no capture has been summarized."""
-    f = ROOT / "profiles" / "gemv_oneshot_m1_sweep_dram.md"
+    """DRAM bytes (read + write) per launch of the decode GEMV over one sweep step, as last measured by ncu on this
+    build's kernel (profiles/traffic.json: the figure, the kernel and the capture command), or None."""
+    f = ROOT / "profiles" / "traffic.json"
     if not f.exists():
         return None
-    for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+    try:
+        return float(json.loads(f.read_text())["traffic_bytes_per_launch"])
+    except (ValueError, KeyError):
+        return None
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -184,24 +197,75 @@ def capture(fn):
     return g, out
 
 
-def per_shape(ops, quant, device, peak):
+_T0 = time.perf_counter()
+
+
+def progress(rank, what):
+    """One line per benchmark leg on stderr (rank 0), so a run that dies shows where."""
+    if rank == 0:
+        print(f"[bench {time.perf_counter() - _T0:7.1f} s] {what}", file=sys.stderr, flush=True)
+
+
+def graph_us(run, calls, reps=5, warm=3):
+    """Capture `run` (which makes `calls` kernel calls) as one CUDA graph, replay it `warm` times untimed, then
+    `reps` times between CUDA events on the current stream; the median time per call in microseconds."""
+    g, _ = capture(run)
+    for _ in range(warm):
+        g.replay()
+    st = torch.cuda.current_stream()
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        g.replay()
+        b.record(st)
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3 / calls)
+    del g
+    return statistics.median(times)
+
+
+def reference_kernels():
+    """The reference's own extension (csrc/w4_gemv.cu), built unchanged for sm_100a into oracle/_ref/ -- the
+    per-shape speed bar -- or None when it was not built."""
+    try:
+        from oracle import ref_kernel
+        return ref_kernel.load() if ref_kernel.available() else None
+    except Exception as ex:  # noqa: BLE001 - the bar is reported as missing, the bench still runs
+        print(f"reference kernels unavailable: {ex}", file=sys.stderr)
+        return None
+
+
+MAX_COPIES = 8192   # calls per timed graph: tiny layers (the N = 1 tail: 66 bytes) would otherwise ask for millions
+
+
+def cold_copies(k, n, device, seed, min_bytes=512 << 20):
+    """Enough distinct packed weight + scale copies of an [n, k] layer (mma layout bytes, seeded) that cycling
+    through them reads every call's weights from HBM -- at most MAX_COPIES, which bounds the graph of a tiny layer
+    (whose copies then fit in L2: its time is the call's latency, not its bytes)."""
+    b = n * k // 2 + 2 * n * (k // GROUP)
+    copies = min(MAX_COPIES, max(4, -(-min_bytes // b)))
+    gen = torch.Generator(device=device).manual_seed(seed)
+    packed = torch.randint(0, 256, (copies, n, k // 2), dtype=torch.uint8, device=device, generator=gen)
+    scales = (torch.rand(copies, n, k // GROUP, device=device, generator=gen) * 0.01 + 1e-3).half()
+    return packed, scales, copies
+
+
+def per_shape(ops, quant, device, peak, ref=None):
     """Each projection alone: one graph of calls over >= 512 MiB of distinct copies (4x L2), replayed 5 times;
-    the median per-call time. A model keeps every layer's weights, so copies stand for the layers in between."""
+    the median per-call time. A model keeps every layer's weights, so copies stand for the layers in between.
+    `ref_us`: the reference's gemv_v6 (csrc/w4_gemv.cu:327-391) on the same copies, timed the same way."""
     rows = []
     seen = {}
+    e = ops.ext()
     for model, proj, k, n in projections():
         if (k, n) in seen:
             rows.append(dict(seen[(k, n)], model=model, proj=proj))
             continue
         b = call_bytes(k, n)
-        copies = max(4, -(-(512 << 20) // b))
-        gen = torch.Generator(device=device).manual_seed(k * 31 + n)
-        packed = torch.randint(0, 256, (copies, n, k // 2), dtype=torch.uint8, device=device, generator=gen)
-        scales = (torch.rand(copies, n, k // GROUP, device=device, generator=gen) * 0.01 + 1e-3).half()
-        x = torch.randn(1, k, device=device, generator=gen).half()
+        packed, scales, copies = cold_copies(k, n, device, k * 31 + n)
+        x = torch.randn(1, k, device=device).half()
         y = torch.empty(copies, 1, n, dtype=torch.half, device=device)
-        e = ops.ext()
-        st = torch.cuda.current_stream()
 
         def run():
             for c in range(copies):   # direct C-ABI calls: no host work inside the graph
@@ -209,26 +273,133 @@ def per_shape(ops, quant, device, peak):
                                       n, k, GROUP, 6, 0, torch.cuda.current_stream().cuda_stream)
                 if rc:
                     raise RuntimeError(e.lib.lb_last_error().decode())
-        g, _ = capture(run)
-        for _ in range(3):
-            g.replay()
-        times = []
-        for _ in range(5):
-            a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(st)
-            g.replay()
-            bb.record(st)
-            bb.synchronize()
-            times.append(a.elapsed_time(bb) * 1e3 / copies)
-        us = statistics.median(times)
+        us = graph_us(run, copies)
         row = {"model": model, "proj": proj, "K": k, "N": n, "bytes": b, "us": round(us, 3),
                "gbs": round(b / (us * 1e-6) / 1e9, 1), "frac": round(b / (us * 1e-6) / 1e9 / peak, 3),
                "copies": copies}
+        if ref is not None:
+            rus = graph_us(lambda: [ref.w4_gemv(x, packed[c], scales[c], GROUP, 6, 0) for c in range(copies)], copies)
+            row["ref_us"] = round(rus, 3)
+            row["speedup_vs_ref"] = round(rus / us, 2)
         seen[(k, n)] = row
         rows.append(row)
-        del g, packed, scales, y
+        del packed, scales, y
         torch.cuda.empty_cache()
     return rows
+
+
+SKINNY_M = (2, 4, 8, 16, 32, 48, 64)
+# the reference's tail shapes (K, N): N not a multiple of a tile, K of 128 / 256 / 384 (bench/gpu_run.py:31)
+EDGE_SHAPES = ((128, 1), (256, 1001), (384, 37))
+PREFILL_ROWS = (128, 256, 512, 1024)
+PREFILL_SHAPES = ((2048, 11008), (11008, 2048), (1536, 8960))
+
+
+def unique_shapes():
+    out = []
+    for _, _, k, n in projections():
+        if (k, n) not in out:
+            out.append((k, n))
+    return out
+
+
+def _abi(e, rc):
+    if rc:
+        raise RuntimeError(e.lib.lb_last_error().decode())
+
+
+def skinny(ops, device, peak, ref=None, rows=SKINNY_M, shapes=None):
+    """M in {2, ..., 64} over the config-1 shapes and the tail shapes, every call's weights cold
+    (>= 256 MiB of copies, 2x L2). Per (shape, M): the kernel linear() picks (auto_version), the INT4 tensor-core
+    kernel (version 5) whatever the rule picks, and in the same run the paths it replaces -- dequantize + cuBLAS
+    (the fp16 weight written and read back each call) and cuBLAS on resident fp16 weights -- plus the reference's
+    gemm_v5 (csrc/w4_gemv.cu:215-294) on the same copies (bench/gpu_run.py:250-301)."""
+    from types import SimpleNamespace
+    e = ops.ext()
+    out = []
+    for k, n in shapes or (unique_shapes() + list(EDGE_SHAPES)):
+        progress(0, f"skinny K={k} N={n}")
+        packed, scales, copies = cold_copies(k, n, device, 3 * k + n, min_bytes=256 << 20)
+        c16 = min(MAX_COPIES, max(2, -(-(256 << 20) // (2 * n * k))))
+        w16 = torch.empty(c16, n, k, dtype=torch.half, device=device)
+        for c in range(c16):
+            _abi(e, e.lib.lb_w4_dequant(packed[c].data_ptr(), scales[c].data_ptr(), w16[c].data_ptr(), n, k, GROUP, 2,
+                                        torch.cuda.current_stream().cuda_stream))
+        wbuf = torch.empty(n, k, dtype=torch.half, device=device)      # the dequantize path's fp16 weight
+        proxy = SimpleNamespace(packed_mma=True, packed_v3=None, packed=None, n=n)
+        for m in rows:
+            x = torch.randn(m, k, device=device).half()
+            y = torch.empty(max(copies, c16), m, n, dtype=torch.half, device=device)
+            st = lambda: torch.cuda.current_stream().cuda_stream   # noqa: E731
+
+            def int4(version):
+                fn = e.lib.lb_w4_gemv if version == 6 else e.lib.lb_w4_gemm_tc
+                extra = (6, 0) if version == 6 else (0,)
+                return lambda: [_abi(e, fn(x.data_ptr(), packed[c].data_ptr(), scales[c].data_ptr(), y[c].data_ptr(),
+                                          m, n, k, GROUP, *extra, st())) for c in range(copies)]
+
+            def deq_cublas():
+                for c in range(copies):
+                    _abi(e, e.lib.lb_w4_dequant(packed[c].data_ptr(), scales[c].data_ptr(), wbuf.data_ptr(), n, k,
+                                                GROUP, 2, st()))
+                    torch.mm(x, wbuf.t(), out=y[c])
+            path = ops.auto_version(m, proxy)
+            v5 = graph_us(int4(5), copies)
+            dq = graph_us(deq_cublas, copies)
+            cb = graph_us(lambda: [torch.mm(x, w16[c].t(), out=y[c]) for c in range(c16)], c16)
+            us = v5 if path == 5 else dq if path is None else graph_us(int4(path), copies)
+            b = call_bytes(k, n, m)
+            row = {"K": k, "N": n, "M": m, "path": {5: "v5 tensor-core", 6: "v6 GEMV", None: "dequant+cublas"}[path],
+                   "us": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                   "frac": round(b / (us * 1e-6) / 1e9 / peak, 3), "int4_v5_us": round(v5, 3),
+                   "dequant_cublas_us": round(dq, 3), "cublas_fp16_us": round(cb, 3),
+                   "vs_dequant_cublas": round(dq / us, 2), "vs_cublas_fp16": round(cb / us, 2),
+                   "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 2)}
+            if ref is not None:
+                rus = graph_us(lambda: [ref.w4_gemm_tc(x, packed[c], scales[c], GROUP, 0) for c in range(copies)],
+                               copies)
+                row["ref_us"] = round(rus, 3)
+                row["speedup_vs_ref"] = round(rus / us, 2)
+            out.append(row)
+            del y
+        del packed, scales, w16, wbuf
+        torch.cuda.empty_cache()
+    return out
+
+
+def dequant_leg(ops, device, peak):
+    """North-star subsystem 3, the prefill path: the dequantize kernel alone on every config-1 shape (bytes
+    N*K/2 + N*K/64 read + 2*N*K written, cold copies), and at 128..1024 rows linear() -- dequantize + cuBLAS --
+    against cuBLAS on resident fp16 weights (the reference's prefill table, results/RESULTS.md:97-108)."""
+    e = ops.ext()
+    kern = []
+    for k, n in unique_shapes():
+        packed, scales, copies = cold_copies(k, n, device, 5 * k + n, min_bytes=256 << 20)
+        wbuf = torch.empty(2, n, k, dtype=torch.half, device=device)
+        us = graph_us(lambda: [_abi(e, e.lib.lb_w4_dequant(packed[c].data_ptr(), scales[c].data_ptr(),
+                                                           wbuf[c & 1].data_ptr(), n, k, GROUP, 2,
+                                                           torch.cuda.current_stream().cuda_stream))
+                               for c in range(copies)], copies)
+        b = n * k // 2 + n * k // 64 + 2 * n * k
+        kern.append({"K": k, "N": n, "bytes": b, "us": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                     "frac": round(b / (us * 1e-6) / 1e9 / peak, 3)})
+        del packed, scales, wbuf
+        torch.cuda.empty_cache()
+    prefill = []
+    for k, n in PREFILL_SHAPES:
+        wq = ops.W4Weight.from_float(torch.randn(n, k, device=device) * 0.02, GROUP, ("mma",))
+        w16 = ops.dequant(wq, "mma")
+        for m in PREFILL_ROWS:
+            x = torch.randn(m, k, device=device).half()
+            lin = graph_us(lambda: [ops.linear(x, wq) for _ in range(8)], 8)
+            cb = graph_us(lambda: [torch.nn.functional.linear(x, w16) for _ in range(8)], 8)
+            prefill.append({"K": k, "N": n, "M": m, "dequant_cublas_us": round(lin, 2), "cublas_fp16_us": round(cb, 2),
+                            "ratio": round(lin / cb, 3)})
+        del wq, w16
+        torch.cuda.empty_cache()
+    return {"kernel": kern, "prefill": prefill,
+            "note": "prefill rows: one weight, back-to-back calls (the fp16 weight of cuBLAS stays partly in L2, as in "
+                    "a prefill that reuses it); kernel rows: cold copies"}
 
 
 def run_ours(args, rank, world, local):
@@ -236,11 +407,7 @@ def run_ours(args, rank, world, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    dist = init_dist(device) if world > 1 else None
 
     e = ops.ext()
     e.set_option("pdl", 1)
@@ -336,12 +503,29 @@ def run_ours(args, rank, world, local):
         e2e_ms = float(t.item())
     e2e_val = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
-    shapes = None
-    if rank == 0 and not args.no_per_shape:
-        del set_graphs, all_graph
-        sets = None
-        torch.cuda.empty_cache()
-        shapes = per_shape(ops, quant, device, peak)
+    # the other configurations, measured after the timed sweep in the same run: the single-GPU kernel legs
+    # (per-shape M = 1, config 2, prefill dequantize) at one GPU; the decoders at every N (config 3 as replicas,
+    # config 4 sharded over all ranks)
+    del set_graphs, all_graph
+    sets = None
+    torch.cuda.empty_cache()
+    extras = {}
+    ref = reference_kernels() if world == 1 else None
+    if world == 1 and not args.no_per_shape:
+        progress(rank, "per_shape")
+        extras["per_shape"] = per_shape(ops, quant, device, peak, ref)
+    if world == 1 and not args.no_skinny:
+        progress(rank, "skinny")
+        extras["skinny"] = skinny(ops, device, peak, ref)
+    if world == 1 and not args.no_dequant:
+        progress(rank, "dequant")
+        extras["dequant"] = dequant_leg(ops, device, peak)
+    if not args.no_decode:
+        progress(rank, "decode_3b")
+        extras["decode_3b"] = decode_summary(run_decode(args, rank, world, local, dist, steps=128, warm=16))
+        progress(rank, "tp_decode")
+        extras["tp_decode"] = decode_summary(run_tp_decode(args, rank, world, local, dist, steps=128, warm=16))
+    progress(rank, "legs done")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(budget_s=args.cpu_seconds)
@@ -393,24 +577,38 @@ def run_ours(args, rank, world, local):
                        "copy inside the timed region; stream synchronized at the end of each step"},
         "gpu_launches": launches_per_step * args.steps,
     }
-    if shapes is not None:
-        line["per_shape"] = shapes
+    line.update({k: v for k, v in extras.items() if v is not None})
+    if ref is None and world == 1:
+        line["reference_kernels"] = "unavailable: oracle/_ref was not built (no reference checkout at build time)"
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
+
+
+def decode_summary(line):
+    """The sub-record of a decoder run (configs 3 and 4) inside the headline line (rank 0; None elsewhere)."""
+    if line is None:
+        return None
+    rf = line["roofline"]
+    return {"metric": line["metric"], "value": line["value"], "unit": line["unit"], "n_gpus": line["n_gpus"],
+            "ms_per_token": line["ms_per_step"], "steps": line["steps"], "warmup": line["warmup"],
+            "scaling": line["scaling"], "parallelism": line["config"]["parallelism"], "fuse": line["config"]["fuse"],
+            "roofline": {k: rf[k] for k in rf if k != "traffic"}, "e2e": line["e2e"], "clocks": line["clocks"],
+            "gpu_launches": line["gpu_launches"]}
 
 
 # ------------------------------------------------------------------------------------------------ CPU arm
 
 def cpu_sweep_inputs(seed=0):
     """The same workload on the host: the 21 projections, packed canonical weights + scales (CPU tensors)."""
+    from lowbit import quant
     g = torch.Generator().manual_seed(seed)
     out = []
     for _, _, k, n in projections():
-        packed = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g)
-        scales = (torch.rand(n, k // GROUP, generator=g) * 0.01 + 1e-3).half()
+        # the GPU arm's weights: N(0, 0.02), quantized to the lowbit format (absmax, group 128)
+        packed, scales = quant.quantize_w4((torch.randn(n, k, generator=g) * 0.02).numpy(), GROUP)
         x = torch.randn(1, k, generator=g).half()
-        out.append((x, packed, scales, k, n))
+        out.append((x, torch.from_numpy(packed), torch.from_numpy(scales), k, n))
     return out
 
 
@@ -478,7 +676,7 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantize to fp16, fp32 matmul)",
-        "data": "synthetic: seeded packed weights, N(0, 1) activations",
+        "data": "synthetic: seeded N(0, 0.02) weights quantized by lowbit's format, N(0, 1) activations",
         "config": {"workload": "BASELINE config 1 on the host: the 21 Qwen2.5 projections, M=1", "M": 1,
                    "bytes_per_step": step_bytes, "parallelism": "host cores, rank 0 only"},
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -507,28 +705,38 @@ def profile_case(k, n, m, copies=8, calls=6):
 DECODE_CONTEXT = 512
 
 
-def run_decode(args, rank, world, local):
+def init_dist(device, timeout_s=600):
+    """The NCCL process group of a torchrun job (one rank per GPU), with a bounded timeout."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=device)
+    return dist
+
+
+def run_decode(args, rank, world, local, dist=None, steps=None, warm=None):
     """Config 3: random-init Qwen2.5-3B architecture, all 252 projections INT4 group-128, batch-1 greedy decode with
     one CUDA graph per step (embedding -> 36 layers -> tied fp16 lm_head -> argmax) after a 512-token prompt of
     ids uniform over the vocabulary. value = tokens/s on the device; e2e also reads every token back to the host,
     as a streaming generator does. N > 1: independent replicas (the model fits one GPU; config 4 is the sharded
-    one)."""
+    one). `dist`: an initialized torch.distributed module (None: this call makes and ends its own group)."""
     from lowbit import decode
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    own = dist is None and world > 1
+    if own:
+        dist = init_dist(device)
     decode.enable_decode_options()
-    steps, warm = min(args.steps, 256), min(args.warmup, 64)
+    steps = steps or min(args.steps, 256)
+    warm = warm or min(args.warmup, 64)
+    fuse = fuse_arg(args, 3)
     m = decode.build(decode.QWEN25_3B, seed=rank)
-    dec = decode.Int4Decoder(m, DECODE_CONTEXT + warm + 2 * steps + 16, fuse=fuse_arg(args))
+    dec = decode.Int4Decoder(m, DECODE_CONTEXT + warm + 2 * steps + 16, fuse=fuse)
+    del m
+    torch.cuda.empty_cache()
     int4_bytes = dec.int4_bytes
     gen = torch.Generator().manual_seed(7 + rank)
-    prompt = torch.randint(0, m.config.vocab_size, (DECODE_CONTEXT,), generator=gen)
+    prompt = torch.randint(0, decode.QWEN25_3B["vocab_size"], (DECODE_CONTEXT,), generator=gen)
     dec.prefill(prompt)
     for _ in range(warm):
         dec.step()
@@ -568,11 +776,12 @@ def run_decode(args, rank, world, local):
         "metric": "Qwen2.5-3B decode tokens/s (batch 1, greedy, one CUDA graph per step, 512-token context)",
         "value": round(tok_s * world, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 weights x fp16 activations, fp32 accumulate", "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
+        "dtype": "int4 weights x fp16 activations, fp32 accumulate",
+        "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
         "config": {"workload": "config 3: Qwen2.5-3B architecture, 36 layers, 252 INT4 projections, tied fp16 lm_head",
                    "model": "Qwen2.5-3B (random init)", "global_batch": world, "seq_len": DECODE_CONTEXT,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "weights 2 GB per token >> 126 MB L2", "fuse": list(fuse_arg(args))},
+                   "l2": "weights 2 GB per token >> 126 MB L2", "fuse": list(fuse)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_bytes_per_token": per_tok,
@@ -585,7 +794,10 @@ def run_decode(args, rank, world, local):
     }
     if dist:
         dist.barrier()
-        dec.graph = None
+    dec.graph = None
+    del dec
+    torch.cuda.empty_cache()
+    if own:
         dist.destroy_process_group()
     return line if rank == 0 else None
 
@@ -595,25 +807,27 @@ def run_decode(args, rank, world, local):
 TP_CONTEXT = 1024
 
 
-def run_tp_decode(args, rank, world, local):
+def run_tp_decode(args, rank, world, local, dist=None, steps=None, warm=None):
     """Config 4: random-init Qwen2.5-7B architecture, INT4 group-128, tensor-parallel over the torchrun ranks
-    (column-parallel q|k|v and gate|up, row-parallel o and down + NCCL allreduce, vocabulary-parallel lm_head),
+    (column-parallel q|k|v and gate|up, row-parallel o and down + allreduce, vocabulary-parallel lm_head),
     batch-1 greedy decode with one CUDA graph per step after a 1024-token prompt. value = tokens/s of the whole
-    job (strong scaling: the same model split over more GPUs), timed on the device, max over ranks."""
+    job (strong scaling: the same model split over more GPUs), timed on the device, max over ranks. At one GPU the
+    unsharded model. `dist`: an initialized torch.distributed module (None: this call makes and ends its own)."""
     from lowbit import decode
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    own = dist is None and world > 1
+    if own:
+        dist = init_dist(device)
     decode.enable_decode_options()
-    steps, warm = min(args.steps, 256), min(args.warmup, 64)
+    steps = steps or min(args.steps, 256)
+    warm = warm or min(args.warmup, 64)
+    fuse = fuse_arg(args, 4)
+    allreduce = getattr(args, "allreduce", "oneshot")
     m = decode.build(decode.QWEN25_7B, seed=0, device=device)
     dec = decode.Int4Decoder(m, TP_CONTEXT + warm + steps + 16, world=world, rank=rank,
-                             pg=dist.group.WORLD if dist else None, allreduce=args.allreduce, fuse=fuse_arg(args))
+                             pg=dist.group.WORLD if dist else None, allreduce=allreduce, fuse=fuse)
     del m
     torch.cuda.empty_cache()
     gen = torch.Generator().manual_seed(7)
@@ -652,9 +866,10 @@ def run_tp_decode(args, rank, world, local):
         "data": "synthetic: random-init weights (N(0, 0.02)), prompt ids uniform over the vocabulary",
         "config": {"workload": "config 4: Qwen2.5-7B architecture, 28 layers, INT4 group-128, untied fp16 lm_head",
                    "model": "Qwen2.5-7B (random init)", "global_batch": 1, "seq_len": TP_CONTEXT,
-                   "parallelism": f"tp{world}: column q|k|v, gate|up; row o, down + "
-                                  f"{'one-shot peer-memory' if args.allreduce == 'oneshot' else 'NCCL'} allreduce; "
-                                  "vocab lm_head", "fuse": list(fuse_arg(args))},
+                   "parallelism": (f"tp{world}: column q|k|v, gate|up; row o, down + "
+                                   f"{'one-shot peer-memory' if allreduce == 'oneshot' else 'NCCL'} allreduce; "
+                                   "vocab lm_head") if world > 1 else "single GPU (unsharded)",
+                   "fuse": list(fuse)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_bytes_per_token_per_rank": per_rank,
@@ -666,8 +881,11 @@ def run_tp_decode(args, rank, world, local):
     }
     if dist:
         dist.barrier()
-        dec.graph = None
-        torch.cuda.synchronize()
+    dec.graph = None
+    del dec
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if own:
         dist.destroy_process_group()
     return line if rank == 0 else None
 
@@ -698,12 +916,12 @@ def profile_sweep(passes=2):
 DEFAULT_FUSE = {3: "", 4: "epilogue,gemv_allreduce"}
 
 
-def fuse_arg(args):
+def fuse_arg(args, config=None):
     """--fuse: comma-separated kernel fusions of the decode step (Int4Decoder's `fuse`); the config's measured
     default when not given."""
     f = getattr(args, "fuse", None)
     if f is None:
-        f = DEFAULT_FUSE.get(getattr(args, "config", 3), "")
+        f = DEFAULT_FUSE.get(config or getattr(args, "config", 3), "")
     return tuple(x for x in f.split(",") if x)
 
 
@@ -731,6 +949,9 @@ def main():
                     help="1: M=1 GEMV sweep over the Qwen2.5 projections (headline); 3: Qwen2.5-3B decode tok/s; "
                          "4: Qwen2.5-7B tensor-parallel decode tok/s over the torchrun ranks")
     ap.add_argument("--no-per-shape", action="store_true")
+    ap.add_argument("--no-skinny", action="store_true", help="skip the config-2 sweep (M = 2..64)")
+    ap.add_argument("--no-dequant", action="store_true", help="skip the prefill dequantize leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 and config-4 decoder legs")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",

@@ -136,7 +136,7 @@ LB_API int lb_w4_repack(const void* canonical, void* dst, int64_t n, int64_t k, 
  *                      part_o (fp32, nh * lb_decode_attention_splits(max_len) * hd) and part_ml (fp32, twice
  *                      nh * splits) are caller-owned scratch; qkv, bias, inv_freq, the caches and part_o 16-byte
  *                      aligned, part_ml 8-byte aligned; hd a multiple of
- *                      8 (<= 1024), max_len <= 65536; the cache rows below pos, bias and inv_freq are read before the
+ *                      8 in 32..1024, max_len <= 65536; the cache rows below pos, bias and inv_freq are read before the
  *                      kernel waits on the previous kernel in the stream (they must not be its output); a pos outside
  *                      0..max_len-1 writes nothing and sets lb_device_error() to 3
  * lb_decode_silu_mul:  a[I] = fp16(silu(gu[i])) * gu[I + i]     (gu = [gate | up])
@@ -166,7 +166,9 @@ LB_API int lb_decode_gemv_fusable(int64_t n, int64_t k);
  * bufs: device array of `world` pointers, bufs[r] = rank r's peer-mapped buffer: 256 bytes of epoch flags (zero
  * at setup) then two slots of `cap` fp16. epoch: this rank's uint32 device counter (zero at setup), advanced by
  * each call. Every rank must make the same sequence of calls. A rank waits about a second for its peers, then
- * records 2 in the device status word (lb_device_error) and gives up instead of hanging. out may alias in; n and
+ * records 2 in the device status word (lb_device_error) and gives up instead of hanging: it then writes none of its
+ * outputs and does not advance its epoch, so the ranks no longer agree and the group must be set up again. A caller
+ * that cannot rule out a missing peer checks lb_device_error() before using the outputs. out may alias in; n and
  * cap are multiples of 8, in and out 16-byte aligned.
  */
 LB_API int lb_tp_allreduce(const void* in, void* out, int64_t n, int64_t cap, void* const* bufs, uint32_t* epoch,
@@ -186,7 +188,8 @@ LB_API int lb_tp_allreduce_norm(const void* in, int64_t n, int64_t cap, void* co
  * lb_tp_allreduce_norm); h_out = norm_w * fp16(x_res * rsqrt(mean(x_res^2) + eps)); y (may be null) receives the
  * sum. Each finished 16-row tile is stored over NVLink into every rank's buffer as it completes, as 8-byte words
  * (epoch << 32 | two fp16 outputs) that validate themselves; the last CTA polls only local memory until every
- * rank's words carry the epoch (at most ~1 s, then lb_device_error() = 2). bufs[r]: rank r's peer-mapped buffer
+ * rank's words carry the epoch (at most ~1 s, then lb_device_error() = 2, and y, x_res and h_out are left as they
+ * were, as in lb_tp_allreduce). bufs[r]: rank r's peer-mapped buffer
  * of 256 bytes of header + 2 * world * cap * 4 bytes (zeroed before first use, not shared with lb_tp_allreduce),
  * epoch: this rank's device counter (equal on every rank), counter: a device int, zero before the first call.
  */
@@ -228,7 +231,8 @@ LB_API int lb_decode_swiglu_gemv(const void* gu, const void* w, const void* scal
  * combine step reads is written first by the same call. The scratch is one per device and shared by every call on
  * it: calls that can run at the same time (different streams, or host threads without ordering between them)
  * race on it, so the caller must serialize them. The first call on each device resolves the scratch address with
- * cudaGetSymbolAddress; make that first call outside any stream capture.
+ * cudaGetSymbolAddress; make that first call outside any stream capture. The address is kept for the life of the
+ * process: do not use this entry point on a device after cudaDeviceReset of that device.
  */
 LB_API int lb_decode_attention_noalloc(const void* qkv, const void* bias, const float* inv_freq, const int64_t* pos,
                                 void* k_cache, void* v_cache, void* out, int nh, int nkv, int hd, int64_t max_len,

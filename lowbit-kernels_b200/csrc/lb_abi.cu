@@ -365,8 +365,9 @@ int lb_decode_rmsnorm(void* x, const void* r, const void* w, void* h, int64_t H,
 
 static int check_heads(int nh, int nkv, int hd, int64_t max_len) {
   if (nh <= 0 || nkv <= 0 || nh % nkv) return fail(LB_ERR_ARGUMENT, "head counts %d / %d", nh, nkv);
-  if (hd <= 0 || hd % 8 || hd > 1024)
-    return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8 and <= 1024", hd);
+  // the combine step runs one thread per head dimension and reduces with full-warp shuffles: at least one warp
+  if (hd < 32 || hd % 8 || hd > 1024)
+    return fail(LB_ERR_ARGUMENT, "head dim %d must be a multiple of 8 in 32..1024", hd);
   if (max_len <= 0 || max_len > lb::attn_max_len())
     return fail(LB_ERR_ARGUMENT, "cache length %lld must be in 1..%d", (long long)max_len, lb::attn_max_len());
   if (lb::attn_smem_bytes(nh, nkv, hd) > 227 * 1024)

@@ -70,6 +70,9 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const __h
       !wait_peer_epoch(reinterpret_cast<const uint32_t*>(mine) + threadIdx.x, e, &g_ar_status))
     timed_out = 1;
   __syncthreads();
+  // a peer that never published: write nothing (out, x_res and h_out keep their values, the epoch does not advance)
+  // and leave the status word at 2 for the host
+  if (timed_out) return;
   float ss_part = 0.f;
   for (int v = threadIdx.x; v < n8; v += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

@@ -633,6 +633,28 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     // piece v of the finished output row: y as stored above, or the rank-ordered fp32 sum of the ranks' words
     // (each polled, for at most ~1 s in all, until it carries this epoch)
     const long long t_wait = clock64();
+    if constexpr (EPI == 3) {
+      // every rank's words of this thread's pieces carry the epoch, or the wait ran out: then nothing is written
+      // (y, x_res and h keep their values, the epoch does not advance) and the status word holds 2 for the host
+      for (int v = threadIdx.x; v < N / 8 && !timed_out; v += blockDim.x) {
+        const uint64_t* base = reinterpret_cast<const uint64_t*>(p.ar_bufs[p.ar_rank] + kPeerFlagBytes) +
+                               (size_t)(ep & 1) * p.ar_world * (p.ar_cap / 2) + 4 * (size_t)v;
+        for (int r = 0; r < p.ar_world && !timed_out; ++r)
+          for (int k = 0; k < 4; ++k)
+            while ((uint32_t)(ld_volatile_u64(base + (size_t)r * (p.ar_cap / 2) + k) >> 32) != ep) {
+              if (clock64() - t_wait > kPeerWaitCycles) {
+                atomicExch(&g_device_status, kErrPeerTimeout);
+                timed_out = 1;
+                break;
+              }
+            }
+      }
+      __syncthreads();
+      if (timed_out) {
+        if (threadIdx.x == 0) *p.epi_counter = 0;
+        return;
+      }
+    }
     auto y_piece = [&](int v) -> uint4 {
       if constexpr (EPI == 2) {
         return ldg_cg_u4(p.y + 8 * (size_t)v);

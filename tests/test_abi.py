@@ -108,3 +108,14 @@ def test_quantize_and_repack_rejections(lib):
     assert lib.lb_w4_repack(A, A + 8, 4, 256, 2, None) == 1
     assert b"overlap" in lib.lb_last_error()
     assert lib.lb_w4_repack(A, A + 0x100000, 4, 256, 0, None) == 1
+
+
+@pytest.mark.parametrize("hd", [8, 16, 24])
+def test_attention_refuses_head_dims_below_one_warp(lib, hd):
+    """The combine step runs one thread per head dimension with full-warp shuffle reductions, so head dims below
+    32 are refused up front by both attention entry points, before any CUDA call."""
+    A = FakePtr.A
+    assert lib.lb_decode_attention(A, None, A, A, A, A, A, A, A, 4, 2, hd, 64, None) == 1
+    assert b"32..1024" in lib.lb_last_error()
+    assert lib.lb_decode_attention_noalloc(A, None, A, A, A, A, A, 4, 2, hd, 64, None) == 1
+    assert b"32..1024" in lib.lb_last_error()
