@@ -344,18 +344,23 @@ def skinny(ops, device, peak, ref=None, rows=SKINNY_M, shapes=None):
                                                 GROUP, 2, st()))
                     torch.mm(x, wbuf.t(), out=y[c])
             path = ops.auto_version(m, proxy)
-            v5 = graph_us(int4(5), copies)
+            arms = {}
+            if m <= ops.MAX_ROWS[6]:
+                arms[6] = graph_us(int4(6), copies)
+            if m <= ops.MAX_ROWS[5]:
+                arms[5] = graph_us(int4(5), copies)
             dq = graph_us(deq_cublas, copies)
             cb = graph_us(lambda: [torch.mm(x, w16[c].t(), out=y[c]) for c in range(c16)], c16)
-            us = v5 if path == 5 else dq if path is None else graph_us(int4(path), copies)
+            us = dq if path is None else arms[path]
             b = call_bytes(k, n, m)
             row = {"K": k, "N": n, "M": m, "path": {5: "v5 tensor-core", 6: "v6 GEMV", None: "dequant+cublas"}[path],
                    "us": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
-                   "frac": round(b / (us * 1e-6) / 1e9 / peak, 3), "int4_v5_us": round(v5, 3),
-                   "dequant_cublas_us": round(dq, 3), "cublas_fp16_us": round(cb, 3),
-                   "vs_dequant_cublas": round(dq / us, 2), "vs_cublas_fp16": round(cb / us, 2),
-                   "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 2)}
-            if ref is not None:
+                   "frac": round(b / (us * 1e-6) / 1e9 / peak, 3)}
+            row.update({f"v{v}_us": round(t, 3) for v, t in arms.items()})
+            row.update({"dequant_cublas_us": round(dq, 3), "cublas_fp16_us": round(cb, 3),
+                        "vs_dequant_cublas": round(dq / us, 2), "vs_cublas_fp16": round(cb / us, 2),
+                        "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 2)})
+            if ref is not None and m <= 64:
                 rus = graph_us(lambda: [ref.w4_gemm_tc(x, packed[c], scales[c], GROUP, 0) for c in range(copies)],
                                copies)
                 row["ref_us"] = round(rus, 3)
@@ -365,6 +370,31 @@ def skinny(ops, device, peak, ref=None, rows=SKINNY_M, shapes=None):
         del packed, scales, w16, wbuf
         torch.cuda.empty_cache()
     return out
+
+
+SWEEP_ROWS = (1, 2, 4, 8, 12, 16, 24, 32, 48, 64, 96, 128, 256)
+
+
+def sweep_dispatch(out_path):
+    """The record linear()'s dispatch table is derived from (lowbit/dispatch.py): every config-1 shape at M = 1..256,
+    cold weights, version 6 / version 5 / dequantize + cuBLAS / fp16 cuBLAS per cell. Writes the record and prints
+    the table it implies."""
+    from lowbit import dispatch, ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    e = ops.ext()
+    e.set_option("pdl", 1)
+    e.set_option("early_weights", 1)
+    peak, _ = measured_peak()
+    t0 = time.time()
+    cells = skinny(ops, device, peak, None, rows=SWEEP_ROWS, shapes=unique_shapes())
+    table = dispatch.derive(cells)
+    rec = {"device": torch.cuda.get_device_name(), "date": time.strftime("%Y-%m-%d"), "wide_n": 3072,
+           "seconds": round(time.time() - t0), "table": table,
+           "how": "bench.py --sweep-dispatch: per (shape, M) the per-call time with cold weights (>= 256 MiB of "
+                  "copies, one CUDA graph per cell, median of 5 replays)", "cells": cells}
+    pathlib.Path(out_path).write_text(json.dumps(rec, indent=1) + "\n")
+    print(json.dumps(table))
 
 
 def dequant_leg(ops, device, peak):
@@ -960,11 +990,16 @@ def main():
                     help="configs 3, 4: decode-step fusions, comma-separated: epilogue (norms and SwiGLU in the "
                          "GEMV / allreduce epilogues), gemv_allreduce (config 4: o and down GEMVs fused with their "
                          "allreduce) or any of qkv, gu, down (GEMV prologues); --fuse= for none")
+    ap.add_argument("--sweep-dispatch", default=None, metavar="OUT.json",
+                    help="sweep the config-1 shapes at M = 1..256 and write the record the dispatch table follows from")
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",
                     help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
+    if args.sweep_dispatch:
+        sweep_dispatch(args.sweep_dispatch)
+        return
     if args.profile_decode:
         profile_decode(fuse_arg(args))
         return

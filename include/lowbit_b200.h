@@ -95,6 +95,15 @@ LB_API int lb_w4_gemm_tc(const void* x, const void* w, const void* scales, void*
                   int64_t group, int row_tiles, lb_stream_t stream);
 
 /*
+ * y[M, N] = x[M, K] * dequant(W)^T + bias, the bias added in the kernel's epilogue: each output is the product
+ * rounded to fp16, plus bias[n] (fp16 [N], 2-byte aligned; NULL for none), rounded again -- the bits of the
+ * reference's W4Linear.forward, which adds the bias to the kernel's fp16 output (lowbit/model.py:22-27).
+ * version 1..4 or 6: the checks and kernels of lb_w4_gemv (M <= 8); version 5: those of lb_w4_gemm_tc (M <= 64).
+ */
+LB_API int lb_w4_linear(const void* x, const void* w, const void* scales, const void* bias, void* y, int64_t m,
+                        int64_t n, int64_t k, int64_t group, int version, lb_stream_t stream);
+
+/*
  * out[N, K] fp16 = fp16_rn((u - 8) * scale), bit-identical to the reference's dequantize kernels.
  * Replaces w4_dequant(w, s, group, mma_layout) (csrc/w4_gemv.cu:517-540); layout is an lb_layout
  * (the reference's mma_layout=False/True are LB_LAYOUT_CANONICAL / LB_LAYOUT_MMA).

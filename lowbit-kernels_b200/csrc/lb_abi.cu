@@ -172,10 +172,11 @@ lb::OneshotConfig unsplit_config(int N, int K) {
 }
 
 int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m, int64_t n, int64_t k,
-                 int64_t group, cudaStream_t st) {
+                 int64_t group, cudaStream_t st, const void* bias = nullptr) {
   lb::GemvParams p{x, w, s, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group,
                    g_opt[LB_OPT_EARLY_WEIGHTS].load() ? (int)lb::kFlagEarlyWeights : 0, 1, (int)(k / group),
                    (int)(group / 128)};
+  p.bias = static_cast<const __half*>(bias);
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
   if (kernel == 2 || (kernel == 0 && m > 16)) {
     // tcgen05: per 128-row tile a cluster of CTAs splitting K, tensor-memory accumulators
@@ -194,10 +195,10 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
       return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
     const int64_t h = (m / 2 + 7) & ~7LL;   // keep the first half a whole number of 8-row tiles
     const int64_t m0 = h < m ? h : m / 2;
-    int rc = run_gemv_mma(x, w, s, y, m0, n, k, group, st);
+    int rc = run_gemv_mma(x, w, s, y, m0, n, k, group, st, bias);
     if (rc) return rc;
     return run_gemv_mma(static_cast<const char*>(x) + m0 * k * 2, w, s, static_cast<char*>(y) + m0 * n * 2, m - m0,
-                        n, k, group, st);
+                        n, k, group, st, bias);
   }
   return launched(lb::launch_gemv_mma(p, c, st), "w4_gemv");
 }
@@ -245,8 +246,11 @@ int lb_get_option(int option) {
   return g_opt[option].load();
 }
 
-int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
-               int64_t group, int version, int rows_per_warp, lb_stream_t stream) {
+}  // extern "C"
+
+// lb_w4_gemv's checks and dispatch (csrc/w4_gemv.cu:454-484), with an optional bias for lb_w4_linear
+static int w4_gemv_impl(const void* x, const void* w, const void* scales, const void* bias, void* y, int64_t m,
+                        int64_t n, int64_t k, int64_t group, int version, int rows_per_warp, lb_stream_t stream) {
   int rc = check_common(x, w, scales, y, m, n, k, group);
   if (rc) return rc;
   if (m < 1 || m > 8)
@@ -256,25 +260,47 @@ int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_
     return fail(LB_ERR_ARGUMENT, "v6 needs K and the group size to be multiples of 128");
   if (!(rows_per_warp == 0 || rows_per_warp == 1 || rows_per_warp == 2 || rows_per_warp == 4))
     return fail(LB_ERR_ARGUMENT, "rows_per_warp is 0 (auto), 1, 2 or 4");
+  if (!aligned2(bias)) return fail(LB_ERR_ALIGNMENT, "bias must be 2-byte aligned");
   if ((rc = check_device())) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (version == 6) return run_gemv_mma(x, w, scales, y, m, n, k, group, st);
+  if (version == 6) return run_gemv_mma(x, w, scales, y, m, n, k, group, st, bias);
   lb::GemvParams p{x, w, scales, reinterpret_cast<__half*>(y), (int)m, (int)n, (int)k, (int)group, 0, 1,
                    (int)(k / group), (int)(group / 128)};
+  p.bias = static_cast<const __half*>(bias);
   int R = rows_per_warp ? rows_per_warp : (n >= 512 ? 4 : (m >= 4 ? 2 : 1));
   return launched(lb::launch_gemv_compat(p, R, version >= 3, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemv");
 }
 
-int lb_w4_gemm_tc(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
-                  int64_t group, int row_tiles, lb_stream_t stream) {
+// lb_w4_gemm_tc's checks and dispatch (csrc/w4_gemv.cu:486-515), with an optional bias for lb_w4_linear
+static int w4_gemm_impl(const void* x, const void* w, const void* scales, const void* bias, void* y, int64_t m,
+                        int64_t n, int64_t k, int64_t group, int row_tiles, lb_stream_t stream) {
   int rc = check_common(x, w, scales, y, m, n, k, group);
   if (rc) return rc;
   if (m < 1 || m > 64) return fail(LB_ERR_ARGUMENT, "the tensor-core kernel takes 1..64 rows");
   if (k % 128 || group % 128) return fail(LB_ERR_ARGUMENT, "v5 needs K and the group size to be multiples of 128");
   if (!(row_tiles == 0 || row_tiles == 1 || row_tiles == 2 || row_tiles == 4))
     return fail(LB_ERR_ARGUMENT, "row_tiles must be 1, 2 or 4");
+  if (!aligned2(bias)) return fail(LB_ERR_ALIGNMENT, "bias must be 2-byte aligned");
   if ((rc = check_device())) return rc;
-  return run_gemv_mma(x, w, scales, y, m, n, k, group, reinterpret_cast<cudaStream_t>(stream));
+  return run_gemv_mma(x, w, scales, y, m, n, k, group, reinterpret_cast<cudaStream_t>(stream), bias);
+}
+
+extern "C" {
+
+int lb_w4_gemv(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+               int64_t group, int version, int rows_per_warp, lb_stream_t stream) {
+  return w4_gemv_impl(x, w, scales, nullptr, y, m, n, k, group, version, rows_per_warp, stream);
+}
+
+int lb_w4_gemm_tc(const void* x, const void* w, const void* scales, void* y, int64_t m, int64_t n, int64_t k,
+                  int64_t group, int row_tiles, lb_stream_t stream) {
+  return w4_gemm_impl(x, w, scales, nullptr, y, m, n, k, group, row_tiles, stream);
+}
+
+int lb_w4_linear(const void* x, const void* w, const void* scales, const void* bias, void* y, int64_t m, int64_t n,
+                 int64_t k, int64_t group, int version, lb_stream_t stream) {
+  if (version == 5) return w4_gemm_impl(x, w, scales, bias, y, m, n, k, group, 0, stream);
+  return w4_gemv_impl(x, w, scales, bias, y, m, n, k, group, version, 0, stream);
 }
 
 int lb_w4_dequant(const void* w, const void* scales, void* out, int64_t n, int64_t k, int64_t group, int layout,

@@ -113,6 +113,13 @@ __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
 }
 
+// An output value as the reference's W4Linear produces it (lowbit/model.py:22-27): the product rounded to fp16, then,
+// with a bias, the fp16 bias added and the sum rounded again (torch's fp16 add: computed in fp32, rounded once)
+__device__ __forceinline__ __half out_half(float v, const __half* bias, int row) {
+  const __half h = __float2half_rn(v);
+  return bias ? __float2half_rn(__half2float(h) + __half2float(bias[row])) : h;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -81,6 +81,7 @@ struct TcParams {
   int wait_guard;  // always 1 (see pdl_wait_after_loads)
   int splits;      // CTAs per cluster splitting K (gridDim.y)
   int ngroups;     // scale groups staged per CTA (the largest K range's)
+  const __half* bias;   // fp16 [N] added to every output row, or null
 };
 
 // both phases, polled together (each poll of a completed barrier still costs a full shared-memory round trip)
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n0 + row < N) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (col0 + j < M) p.y[(size_t)(col0 + j) * N + n0 + row] = __float2half_rn(__uint_as_float(v[j]));
+            if (col0 + j < M) p.y[(size_t)(col0 + j) * N + n0 + row] = out_half(__uint_as_float(v[j]), p.bias, n0 + row);
         }
       } else {
 #pragma unroll
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float a[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (n0 + row4 + j < N) yo[j] = __float2half_rn(a[j]);
+        if (n0 + row4 + j < N) yo[j] = out_half(a[j], p.bias, n0 + row4 + j);
     }
     cluster_sync_all();   // no CTA leaves while another still reads its partials
   }
@@ -487,7 +488,7 @@ cudaError_t launch_tc_t(const GemvParams& g, int S, bool pdl, cudaStream_t st) {
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
   const int KC = g.K / 128;
-  TcParams p{g.s, g.y, g.M, g.N, g.K, g.KG, g.cpg, g.flags, g.wait_guard, S, groups_per_cta(KC, g.cpg, S)};
+  TcParams p{g.s, g.y, g.M, g.N, g.K, g.KG, g.cpg, g.flags, g.wait_guard, S, groups_per_cta(KC, g.cpg, S), g.bias};
   const cuuint32_t estride[2] = {1, 1};
   // activations as a [M, K] fp16 tensor; boxes of 64 k x NB rows, rows past M are filled with zeros
   CUtensorMap xmap, wmap;

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
       const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
       const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
       const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-      if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+      if (row < N && m < M) p.y[(size_t)m * N + row] = out_half(v, p.bias, row);
     };
     if (nsplit == 1) {
       if (reducer) {
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
     const int r = rm / MT, mt = rm - r * MT;
     const int row = n0 + 16 * r + (ln >> 2) + (i >= 2 ? 8 : 0);
     const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-    if (row < N && m < M) p.y[(size_t)m * N + row] = __float2half_rn(v);
+    if (row < N && m < M) p.y[(size_t)m * N + row] = out_half(v, p.bias, row);
   };
   auto cta_sum = [&](int e) {
     float v = 0.f;
@@ -896,7 +896,7 @@ __global__ void __launch_bounds__(128) gemv_compat_kernel(GemvParams p) {
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       float v = warp_sum(acc[r][m]);
-      if (lane == 0 && n0 + r < N) p.y[(size_t)m * N + n0 + r] = __float2half_rn(v);
+      if (lane == 0 && n0 + r < N) p.y[(size_t)m * N + n0 + r] = out_half(v, p.bias, n0 + r);
     }
 }
 

@@ -22,6 +22,7 @@ struct GemvParams {
   int wait_guard;  // always 1 (see pdl_wait_after_loads)
   int KG;          // K / G, groups per row
   int cpg;         // G / 128, 128-wide chunks per group (mma layout kernels)
+  const __half* bias = nullptr;   // fp16 [N] added to every output row (plain GEMV / GEMM only), or null
   // activation prologue of the one-shot GEMV (M = 1, K unsplit): 0 none; 1 x <- w * fp16((x + r) *
   // rsqrt(mean((x + r)^2) + eps)) with x + r written to out by CTA 0 (r, out may be null); 2 x <- silu(x[0:K]) *
   // x[K:2K] (x is a [gate | up] row of 2K values)

@@ -30,6 +30,7 @@ SIGNATURES = {
     "lb_get_option": ([_I], _I),
     "lb_w4_gemv": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P], _I),
     "lb_w4_gemm_tc": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
+    "lb_w4_linear": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
     "lb_w4_dequant": ([_P, _P, _P, _I64, _I64, _I64, _I, _P], _I),
     "lb_w4_quantize": ([_P, _I, _P, _P, _I64, _I64, _I64, _P, _I, _P], _I),
     "lb_w4_repack": ([_P, _P, _I64, _I64, _I, _P], _I),
@@ -148,6 +149,23 @@ class Ext:
         with _Device(x.device):
             rc = self.lib.lb_w4_gemm_tc(x.data_ptr(), w.data_ptr(), s.data_ptr(), y.data_ptr(), m, n, k, group,
                                         int(row_tiles), torch.cuda.current_stream().cuda_stream)
+        if rc:
+            self._raise(rc)
+        return y
+
+    def w4_linear(self, x, w, s, group, version, bias=None, out=None):
+        """x [M, K] @ dequant(W)^T + bias with the bias added in the kernel epilogue (lb_w4_linear): version 1-4, 6
+        (M <= 8) or 5 (M <= 64). bias: fp16 [N] on the same GPU, or None."""
+        _check(x, w, s, group)
+        m, k, n = x.shape[0], x.shape[1], w.shape[0]
+        if bias is not None and (not bias.is_cuda or bias.device != x.device or bias.dtype != torch.float16
+                                 or bias.dim() != 1 or bias.shape[0] != n or not bias.is_contiguous()):
+            raise RuntimeError(f"bias must be a contiguous float16 [{n}] tensor on {x.device}")
+        y = _out(out, m, n, x.device)
+        with _Device(x.device):
+            rc = self.lib.lb_w4_linear(x.data_ptr(), w.data_ptr(), s.data_ptr(),
+                                       None if bias is None else bias.data_ptr(), y.data_ptr(), m, n, k, group,
+                                       int(version), torch.cuda.current_stream().cuda_stream)
         if rc:
             self._raise(rc)
         return y

@@ -117,13 +117,16 @@ def _current_stream(dev):
     return _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream(dev).cuda_stream
 
 
-def _gemv_fast(x, wq, version, out):
-    """The common decode call with the weight's validated launch arguments cached: cheap checks on x and out, one
-    C call. None when anything is unusual -- the checked path below then handles it (and raises its errors)."""
+def _gemv_fast(x, wq, version, out, bias=None):
+    """The common decode call with the weight's validated launch arguments cached: cheap checks on x, out and bias,
+    one C call. None when anything is unusual -- the checked path below then handles it (and raises its errors)."""
     args = wq.launch_args(version)
     if args is None:
         return None
     w_ptr, s_ptr, dev = args
+    if bias is not None and (type(bias) is not torch.Tensor or bias.dtype != torch.float16 or bias.dim() != 1
+                             or bias.shape[0] != wq.n or bias.get_device() != dev or not bias.is_contiguous()):
+        return None
     if (type(x) is not torch.Tensor or x.dtype != torch.float16 or x.dim() != 2 or x.shape[1] != wq.k
             or x.shape[0] == 0 or x.get_device() != dev or not x.is_contiguous()
             or torch.cuda.current_device() != dev):
@@ -137,7 +140,10 @@ def _gemv_fast(x, wq, version, out):
     else:
         return None
     e = ext()
-    if version == 6:
+    if bias is not None:
+        rc = e.lib.lb_w4_linear(x.data_ptr(), w_ptr, s_ptr, bias.data_ptr(), y.data_ptr(), m, n, wq.k, wq.group,
+                                version, _current_stream(dev))
+    elif version == 6:
         rc = e.lib.lb_w4_gemv(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, wq.k, wq.group, 6, 0,
                               _current_stream(dev))
     else:
@@ -148,18 +154,24 @@ def _gemv_fast(x, wq, version, out):
     return y
 
 
-def gemv(x, wq, version=4, rows_per_warp=0, out=None):
+def gemv(x, wq, version=4, rows_per_warp=0, out=None, bias=None):
     """x [M, K] fp16 -> [M, N] fp16. Versions 1-4 and 6: M <= 8; version 5: M <= 64 (tensor cores).
     Versions 5 and 6 read the same layout (packed_mma), so a model needs only that copy. `out`: an optional
-    contiguous fp16 [M, N] tensor the result is written into (no allocation)."""
+    contiguous fp16 [M, N] tensor the result is written into (no allocation). `bias`: an optional fp16 [N] tensor
+    added in the kernel's epilogue, with the roundings of adding it to the fp16 output afterwards (both are
+    additions to the reference's signature)."""
     if (version == 5 or version == 6) and rows_per_warp == 0 and isinstance(wq, W4Weight):
-        y = _gemv_fast(x, wq, version, out)
+        y = _gemv_fast(x, wq, version, out, bias)
         if y is not None:
             return y
     if version not in NEEDS:
         raise ValueError(f"version must be one of {sorted(NEEDS)}")
     if getattr(wq, NEEDS[version]) is None:
         raise ValueError(f"v{version} reads {NEEDS[version]}, which this W4Weight does not keep")
+    if bias is not None:
+        if rows_per_warp != 0:
+            raise ValueError("rows_per_warp is chosen by the kernel when a bias is fused")
+        return ext().w4_linear(x.contiguous(), getattr(wq, NEEDS[version]), wq.scales, wq.group, version, bias, out)
     if version == 5:
         return ext().w4_gemm_tc(x.contiguous(), wq.packed_mma, wq.scales, wq.group, rows_per_warp, out=out)
     w = wq.packed_mma if version == 6 else wq.packed_v3 if version >= 3 else wq.packed
@@ -251,11 +263,13 @@ def auto_version(m, wq):
     return None
 
 
-def linear(x, wq, max_gemv_rows=8, version=0, out=None):
+def linear(x, wq, max_gemv_rows=8, version=0, out=None, bias=None):
     """Decode (few rows): an INT4 kernel; prefill (many rows): dequantize, then cuBLAS fp16 GEMM. version 0 =
     auto_version; a fixed version runs up to min(max_gemv_rows, its row limit) rows (version 5: 64), and
-    dequantize + cuBLAS above that (lowbit/ops.py:163-178). `out` (an addition to the reference's signature): an
-    optional contiguous fp16 [M, N] tensor that receives the result."""
+    dequantize + cuBLAS above that (lowbit/ops.py:163-178). Additions to the reference's signature: `out`, an
+    optional contiguous fp16 [M, N] tensor that receives the result, and `bias`, an optional fp16 [N] tensor added
+    to the result (in the INT4 kernels' epilogue; after the cuBLAS product on the prefill path) with the roundings
+    of adding it to the fp16 output."""
     m = x.shape[0]
     if m == 0:
         return x.new_empty(0, wq.n) if out is None else out
@@ -266,8 +280,12 @@ def linear(x, wq, max_gemv_rows=8, version=0, out=None):
     else:
         raise ValueError(f"version must be 0 (auto) or one of {sorted(MAX_ROWS)}")
     if v is not None:
+        if bias is not None:
+            return gemv(x, wq, v, out=out, bias=bias)
         return gemv(x, wq, v) if out is None else gemv(x, wq, v, out=out)
     y = torch.nn.functional.linear(x, dequant(wq, "mma" if wq.packed_mma is not None else "canonical"))
+    if bias is not None:
+        y = y + bias
     if out is None:
         return y
     if out.shape != y.shape or out.dtype != y.dtype:

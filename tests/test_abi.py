@@ -119,3 +119,16 @@ def test_attention_refuses_head_dims_below_one_warp(lib, hd):
     assert b"32..1024" in lib.lb_last_error()
     assert lib.lb_decode_attention_noalloc(A, None, A, A, A, A, A, 4, 2, hd, 64, None) == 1
     assert b"32..1024" in lib.lb_last_error()
+
+
+def test_linear_rejections(lib):
+    """lb_w4_linear: the checks of lb_w4_gemv (versions 1-4, 6) or lb_w4_gemm_tc (version 5), and a 2-byte aligned
+    bias; all refused before any CUDA call."""
+    A = FakePtr.A
+    assert lib.lb_w4_linear(A, A, A, FakePtr.U, A, 1, 64, 256, 128, 6, None) == 2
+    assert b"bias" in lib.lb_last_error()
+    assert lib.lb_w4_linear(A, A, A, A, A, 9, 64, 256, 128, 6, None) == 1
+    assert b"1..8 rows" in lib.lb_last_error()
+    assert lib.lb_w4_linear(A, A, A, A, A, 65, 64, 256, 128, 5, None) == 1
+    assert b"1..64 rows" in lib.lb_last_error()
+    assert lib.lb_w4_linear(A, A, A, None, A, 2, 64, 256, 128, 7, None) == 1

@@ -431,3 +431,38 @@ def test_no_kernel_wait_gave_up():
     torch.cuda.synchronize()
     assert ops.ext().lib.lb_device_error() == 0
 
+
+
+# ---------------------------------------------------------------- bias in the epilogue (lb_w4_linear)
+
+@pytest.mark.parametrize("name", ["1.5b.q", "3b.down", "odd_n", "tiny"])
+@pytest.mark.parametrize("m", [1, 3, 8, 16, 24, 64])
+def test_bias_epilogue_matches_separate_add_and_fp64(layers, name, m):
+    """ops.gemv / ops.linear with bias=: bit-identical to the kernel's fp16 output plus the fp16 bias (the
+    reference's W4Linear.forward, lowbit/model.py:22-27), and within the GEMV bar of the fp64 product plus bias."""
+    k, n, w, packed, scales, wq = layers[name]
+    g = torch.Generator().manual_seed(n + m)
+    bias = (torch.randn(n, generator=g) * 0.5).half()
+    x = x_for(m, k, k + 7 * m)
+    xc, bc = x.cuda(), bias.cuda()
+    y64 = ref_y(x, packed, scales, 128) + bias.double().numpy()[None]
+    versions = [5] + ([1, 2, 3, 4, 6] if m <= 8 else [])
+    for v in versions:
+        got = ops.gemv(xc, wq, v, bias=bc)
+        assert torch.equal(got, ops.gemv(xc, wq, v) + bc), (name, m, v)
+        rms = np.sqrt(np.mean(y64 ** 2))
+        err = np.abs(got.double().cpu().numpy() - y64).max() / rms
+        assert err <= NORM_BOUND, (name, m, v, err)
+    lin = ops.linear(xc, wq, bias=bc)
+    assert torch.equal(lin, ops.linear(xc, wq) + bc)
+
+
+def test_bias_on_the_prefill_path_and_refusals():
+    wq = ops.W4Weight.from_float(torch.randn(300, 512))
+    bias = torch.randn(300).half().cuda()
+    x = torch.randn(130, 512).half().cuda()
+    assert torch.equal(ops.linear(x, wq, bias=bias), ops.linear(x, wq) + bias)
+    with pytest.raises(RuntimeError):
+        ops.ext().w4_linear(x[:2], wq.packed_mma, wq.scales, 128, 6, bias=bias[:299].contiguous())
+    with pytest.raises(RuntimeError):
+        ops.ext().w4_linear(x[:2], wq.packed_mma, wq.scales, 128, 6, bias=bias.float())
