@@ -24,18 +24,20 @@ __device__ __forceinline__ uint32_t deq_byte(uint32_t b, uint32_t s2) {
   return hmul2_bits(hsub2_bits((b & 0xFu) | ((b & 0xF0u) << 12) | kMagic, kBias1032), s2);
 }
 
-// layout 0 (canonical) and 1 (v3): thread = one 32-bit word = 8 consecutive k -> one 16-byte store
-template <bool V3>
-__global__ void dequant_linear_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                      uint4* __restrict__ out, int N, int K, int G) {
-  const size_t total = (size_t)N * (K >> 3);
+// layout 0 (canonical) and 1 (v3): thread = one 32-bit word = 8 consecutive k -> one 16-byte store; a warp's
+// loads cover 128 contiguous bytes and its stores 512. Idx is 32-bit whenever the layer has fewer than 2^32 words.
+template <bool V3, typename Idx>
+__global__ void __launch_bounds__(256) dequant_linear_kernel(const uint32_t* __restrict__ w,
+                                                             const uint16_t* __restrict__ s, uint4* __restrict__ out,
+                                                             int N, int K, int G) {
+  const Idx per_row = (Idx)(K >> 3), total = (Idx)N * per_row;
   const int KG = K / G;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(idx / (K >> 3));
-    const int k = (int)(idx - (size_t)n * (K >> 3)) * 8;
-    const uint16_t sb = s[(size_t)n * KG + k / G];
+  for (Idx idx = (Idx)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (Idx)gridDim.x * blockDim.x) {
+    const Idx n = idx / per_row;
+    const int k = (int)(idx - n * per_row) * 8;
+    const uint16_t sb = __ldg(s + (size_t)n * KG + k / G);
     const uint32_t s2 = (uint32_t)sb | ((uint32_t)sb << 16);
-    const uint32_t word = w[idx];
+    const uint32_t word = __ldg(w + idx);
     uint4 o;
     if (V3) {
       o.x = deq_pair(word, 0, s2); o.y = deq_pair(word, 1, s2); o.z = deq_pair(word, 2, s2); o.w = deq_pair(word, 3, s2);
@@ -47,44 +49,66 @@ __global__ void dequant_linear_kernel(const uint32_t* __restrict__ w, const uint
   }
 }
 
-// layout 2 (mma): output octet o of a row = k 8o .. 8o + 7 = chunk c = o / 16, ob = o % 16 -> word i = ob / 4,
-// pair j = ob % 4 of the four words t = 0..3 (byte offset 64c + 16t + 4i), whose pair j holds k = 8o + 2t, +1.
-__global__ void dequant_mma_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                   uint4* __restrict__ out, int N, int K, int G) {
-  const size_t total = (size_t)N * (K >> 3);
-  const int KG = K / G;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(idx / (K >> 3));
-    const int o = (int)(idx - (size_t)n * (K >> 3));
-    const int c = o >> 4, ob = o & 15, i = ob >> 2, j = ob & 3;
-    const uint16_t sb = s[(size_t)n * KG + (c * 128) / G];
+// layout 2 (mma). Output octet o of a chunk (k = 8o .. 8o + 7, o = 4i + j) is pair j of word i of the chunk's four
+// 16-byte words t = 0..3 (pair j of word i of word t holds k = 8o + 2t, + 1). Thread (chunk q, pair j) loads the
+// chunk's 64 bytes as four 16-byte loads (the chunk's four threads share them through L1) and writes octets j,
+// 4 + j, 8 + j, 12 + j, so the four threads of a chunk write 64 contiguous bytes per store instruction.
+template <typename Idx>
+__global__ void __launch_bounds__(256) dequant_mma_kernel(const uint4* __restrict__ w, const uint16_t* __restrict__ s,
+                                                          uint4* __restrict__ out, int N, int K, int G) {
+  const Idx KC = (Idx)(K >> 7), total = (Idx)N * KC * 4;
+  const int KG = K / G, cpg = G >> 7;
+  for (Idx idx = (Idx)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (Idx)gridDim.x * blockDim.x) {
+    const Idx q = idx >> 2;        // chunk, row-major over (row, chunk)
+    const int j = (int)(idx & 3);
+    const Idx n = q / KC;
+    const int c = (int)(q - n * KC);
+    const uint16_t sb = __ldg(s + (size_t)n * KG + (cpg == 1 ? c : c / cpg));
     const uint32_t s2 = (uint32_t)sb | ((uint32_t)sb << 16);
-    const uint32_t* src = w + (size_t)n * (K >> 3) + c * 16 + i;   // words of the chunk: 4t + i
-    uint4 r;
-    r.x = deq_pair(__ldg(src + 0), j, s2);
-    r.y = deq_pair(__ldg(src + 4), j, s2);
-    r.z = deq_pair(__ldg(src + 8), j, s2);
-    r.w = deq_pair(__ldg(src + 12), j, s2);
-    out[idx] = r;
+    uint4 wt[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) wt[t] = __ldg(w + (size_t)q * 4 + t);
+    uint4* dst = out + (size_t)q * 16 + j;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 r;
+      r.x = deq_pair((&wt[0].x)[i], j, s2);
+      r.y = deq_pair((&wt[1].x)[i], j, s2);
+      r.z = deq_pair((&wt[2].x)[i], j, s2);
+      r.w = deq_pair((&wt[3].x)[i], j, s2);
+      dst[4 * i] = r;
+    }
   }
 }
 
 static int grid_for(size_t work, int threads) {
   size_t blocks = (work + threads - 1) / threads;
-  const size_t cap = 148 * 32;   // enough resident threads to saturate HBM; larger problems loop
+  const size_t cap = 148 * 8;   // eight 256-thread blocks per SM are resident; larger problems loop
   return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
 cudaError_t launch_dequant(const void* w, const void* s, __half* out, int N, int K, int G, int layout,
                            cudaStream_t st) {
-  const size_t work = (size_t)N * (K >> 3);
-  const int threads = 256, grid = grid_for(work, threads);
-  auto wp = reinterpret_cast<const uint32_t*>(w);
+  const int threads = 256;
   auto sp = reinterpret_cast<const uint16_t*>(s);
   auto op = reinterpret_cast<uint4*>(out);
-  if (layout == 2) dequant_mma_kernel<<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
-  else if (layout == 1) dequant_linear_kernel<true><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
-  else dequant_linear_kernel<false><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+  const bool small = (size_t)N * (size_t)(K >> 3) < (1ull << 31);   // every index fits 32 bits
+  if (layout == 2) {
+    auto wp = reinterpret_cast<const uint4*>(w);
+    const int grid = grid_for((size_t)N * (K >> 7) * 4, threads);
+    if (small) dequant_mma_kernel<uint32_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+    else dequant_mma_kernel<uint64_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+    return cudaGetLastError();
+  }
+  auto wp = reinterpret_cast<const uint32_t*>(w);
+  const int grid = grid_for((size_t)N * (K >> 3), threads);
+  if (layout == 1) {
+    if (small) dequant_linear_kernel<true, uint32_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+    else dequant_linear_kernel<true, uint64_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+  } else {
+    if (small) dequant_linear_kernel<false, uint32_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+    else dequant_linear_kernel<false, uint64_t><<<grid, threads, 0, st>>>(wp, sp, op, N, K, G);
+  }
   return cudaGetLastError();
 }
 
