@@ -52,7 +52,8 @@ typedef enum lb_option {
   LB_OPT_GEMV_WARPS = 3,    /* 0 (default): automatic; 4, 8 or 16 forces the GEMV's warps per CTA */
   LB_OPT_GEMV_DEPTH = 4,    /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
   LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 forces the persistent copy-ring GEMV, 2 the tcgen05
-                               GEMM (any M <= 64) */
+                               GEMM (any M <= 64), 3 the one-shot GEMV with activations staged per CTA (the
+                               automatic choice at M <= 8 stages them per warp, with the same bits) */
   LB_OPT_GEMV_ROWTILES = 6  /* 0 (default): automatic; 1 or 2 forces the one-shot GEMV's 16-row tiles per CTA */
 } lb_option;
 

@@ -34,11 +34,17 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
 //   pair 0: slots 0 and 4 (bits 0-3, 16-19)      -> (1024 + u) - 1032
 //   pair 1: slots 1 and 5 (bits 4-7, 20-23)      -> (1024 + 16u) / 16 - 72
 // Both results are small integers, so every step is exact. Pairs 2 and 3 are the same on (word >> 8).
+// (a & b) | c in one instruction (lop3 truth table 0xEA)
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 __device__ __forceinline__ uint32_t q_pair_lo(uint32_t word) {
-  return hsub2_bits((word & 0x000F000Fu) | kMagic, kBias1032);
+  return hsub2_bits(and_or(word, 0x000F000Fu, kMagic), kBias1032);
 }
 __device__ __forceinline__ uint32_t q_pair_hi(uint32_t word) {
-  return hfma2_bits((word & 0x00F000F0u) | kMagic, kSixteenth, kMinus72);
+  return hfma2_bits(and_or(word, 0x00F000F0u, kMagic), kSixteenth, kMinus72);
 }
 
 // Pair j (0..3) of a v3-order word as exact f16x2 of (u - 8): (k0 + 2j, k0 + 2j + 1)

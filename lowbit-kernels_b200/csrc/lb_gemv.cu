@@ -742,6 +742,174 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   }
 }
 
+// Plain decode GEMV, M <= 8, one 16-row tile and the whole K range per CTA: the arithmetic of gemv_oneshot_kernel
+// at its unsplit, one-row-tile configuration -- the same chunk-to-warp assignment (chunk c to warp c % NW, in
+// order), the same mma.sync sequence per chunk, the same fp32 operations in the same order, so the outputs have
+// its bits -- with less work around it:
+//   * each warp stages only the activations of its own chunks (one 16-byte load and store per lane and 128 k of
+//     a row), so no CTA barrier stands between the wait on the previous kernel and the first mma;
+//   * the only barrier is the one before the cross-warp sum, which covers just the 16 M real outputs of the tile;
+//   * the chunk count per warp and M == 1 are compile-time, so index math and the single-row epilogue fold away.
+template <int CPW, bool EARLY, bool M1>
+__global__ void __launch_bounds__(512) gemv_tile_kernel(GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int NW = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int K = p.K, N = p.N, M = M1 ? 1 : p.M, KC = K >> 7, KG = p.KG, cpg = p.cpg;
+  const int n0 = blockIdx.x * 16;
+  const int xrow = CPW * 256 + 16;             // bytes per activation row in a warp's region (16-byte skew)
+  uint8_t* xw = smem + warp * M * xrow;        // this warp's activations: [M][CPW chunks of 256 bytes]
+  float* red = reinterpret_cast<float*>(smem + NW * M * xrow);   // [NW][16 M] partial sums
+
+  const size_t row_u4 = (size_t)(K >> 5);
+  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N - 1
+  const uint4* wa = reinterpret_cast<const uint4*>(p.w) + (size_t)ra * row_u4 + t;
+  const uint4* wb = reinterpret_cast<const uint4*>(p.w) + (size_t)rb * row_u4 + t;
+  const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
+  const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+
+  uint4 qa[CPW], qb[CPW];
+  uint16_t ssa[CPW], ssb[CPW];
+  pdl_launch_dependents();
+  if (!EARLY) pdl_wait();
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = warp + NW * i;
+    if (c < KC) {
+      const int grp = cpg == 1 ? c : c / cpg;
+      qa[i] = ldg_stream(wa + 4 * c);
+      qb[i] = ldg_stream(wb + 4 * c);
+      ssa[i] = ldg_u16(sa + grp);
+      ssb[i] = ldg_u16(sb + grp);
+    }
+  }
+  if (EARLY) pdl_wait_after_loads(p.wait_guard);
+
+  // this warp's activations: piece (m, i, j) = 16 bytes j of chunk warp + NW i of row m, loaded through L2 (the
+  // previous kernel may just have written them) in rounds of PR pieces per lane -- every load of a round issued
+  // before its first shared-memory store, so a round costs one L2 round trip
+  constexpr int PR = M1 ? (CPW / 2 > 0 ? CPW / 2 : 1) : 4;
+  {
+    const uint8_t* xg = reinterpret_cast<const uint8_t*>(p.x);
+    const int total = M * CPW * 16;
+    for (int base = 0; base < total; base += 32 * PR) {
+      uint4 v[PR];
+      int off[PR];
+#pragma unroll
+      for (int r = 0; r < PR; ++r) {
+        const int e = base + 32 * r + lane;
+        const int m = M1 ? 0 : e / (CPW * 16), rr = M1 ? e : e - m * (CPW * 16), i = rr >> 4, j = rr & 15;
+        const int c = warp + NW * i;
+        off[r] = -1;
+        if (e < total && c < KC) {
+          v[r] = ldg_cg_u4(xg + (size_t)m * K * 2 + (size_t)c * 256 + j * 16);
+          off[r] = m * xrow + i * 256 + j * 16;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < PR; ++r)
+        if (off[r] >= 0) *reinterpret_cast<uint4*>(xw + off[r]) = v[r];
+    }
+  }
+  // the first chunk's fragments are decoded while the activations are in flight
+  uint32_t fr0[4][8];
+#pragma unroll
+  for (int qd = 0; qd < 4; ++qd) {
+    const uint32_t w0 = (&qa[0].x)[qd], w1 = (&qb[0].x)[qd];
+    fr0[qd][0] = q_pair_lo(w0); fr0[qd][1] = q_pair_lo(w1); fr0[qd][2] = q_pair_hi(w0); fr0[qd][3] = q_pair_hi(w1);
+    fr0[qd][4] = q_pair_lo(w0 >> 8); fr0[qd][5] = q_pair_lo(w1 >> 8);
+    fr0[qd][6] = q_pair_hi(w0 >> 8); fr0[qd][7] = q_pair_hi(w1 >> 8);
+  }
+  __syncwarp();
+
+  // ldmatrix row addresses: lane L serves row (L & 7) of 8x8 matrix L >> 3; rows past M repeat row M - 1
+  const uint32_t xaddr = smem_u32(xw + min(lane & 7, M - 1) * xrow + (lane >> 3) * 16);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    if (warp + NW * i < KC) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        uint32_t xb[4];
+        ldsm_x4(xb, xaddr + i * 256 + qd * 64);
+        uint32_t f[8];
+        if (i == 0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = fr0[qd][j];
+        } else {
+          const uint32_t w0 = (&qa[i].x)[qd], w1 = (&qb[i].x)[qd];
+          f[0] = q_pair_lo(w0); f[1] = q_pair_lo(w1); f[2] = q_pair_hi(w0); f[3] = q_pair_hi(w1);
+          f[4] = q_pair_lo(w0 >> 8); f[5] = q_pair_lo(w1 >> 8); f[6] = q_pair_hi(w0 >> 8); f[7] = q_pair_hi(w1 >> 8);
+        }
+        mma16816(d, f[0], f[1], f[2], f[3], xb[0], xb[1]);
+        mma16816(d, f[4], f[5], f[6], f[7], xb[2], xb[3]);
+      }
+      const float s0 = h2f_bits(ssa[i]), s1 = h2f_bits(ssb[i]);
+      acc[0] = fmaf(s0, d[0], acc[0]);
+      acc[2] = fmaf(s1, d[2], acc[2]);
+      if (!M1) {
+        acc[1] = fmaf(s0, d[1], acc[1]);
+        acc[3] = fmaf(s1, d[3], acc[3]);
+      }
+    }
+  }
+  // partial sums of the tile's 16 x M outputs: lane (g, t) holds rows g, g + 8 and activation rows 2t, 2t + 1
+  const int MS = 16 * M;
+  if (M1) {
+    if (t == 0) {
+      red[warp * 16 + g] = acc[0];
+      red[warp * 16 + g + 8] = acc[2];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = 2 * t + (i & 1);
+      if (m < M) red[warp * MS + (g + (i >= 2 ? 8 : 0)) * M + m] = acc[i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < MS; e += blockDim.x) {   // 16 M outputs; a one-warp CTA loops at M > 2
+    float v = 0.f;
+    for (int w = 0; w < NW; ++w) v += red[w * MS + e];
+    const int row = M1 ? e : e / M, m = M1 ? 0 : e - row * M;
+    if (n0 + row < N) p.y[(size_t)m * N + n0 + row] = out_half(v, p.bias, n0 + row);
+  }
+}
+
+size_t tile_smem_bytes(int M, int nw, int cpw) { return (size_t)nw * M * (cpw * 256 + 16) + (size_t)nw * 16 * M * 4; }
+
+template <int CPW, bool M1>
+static cudaError_t launch_tile_t(const GemvParams& p, int nw, bool pdl, cudaStream_t st) {
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_tile_kernel<CPW, true, M1> : gemv_tile_kernel<CPW, false, M1>;
+  const size_t smem = tile_smem_bytes(p.M, nw, CPW);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + 15) / 16, 1, 1);
+  cfg.blockDim = dim3(nw * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+cudaError_t launch_gemv_tile(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
+  if (p.M < 1 || p.M > 8 || c.ksplit != 1 || c.rt != 1 || p.pro || p.epi) return cudaErrorInvalidConfiguration;
+  const bool m1 = p.M == 1;
+#define LB_TILE(CPW_) \
+  if (c.cpw == CPW_) return m1 ? launch_tile_t<CPW_, true>(p, c.warps, c.pdl, st) : launch_tile_t<CPW_, false>(p, c.warps, c.pdl, st);
+  LB_TILE(2) LB_TILE(4) LB_TILE(8)
+#undef LB_TILE
+  return cudaErrorInvalidConfiguration;
+}
+
 template <int MT, int RT, int CPW, int PRO = 0, int EPI = 0>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
   auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true, PRO, EPI>

@@ -72,6 +72,10 @@ struct OneshotConfig {
 };
 cudaError_t launch_gemv_oneshot(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);  // p.pro / p.epi: M = 1, ksplit 1, rt 1
 size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt);
+// the plain M <= 8 GEMV at an unsplit, one-row-tile one-shot configuration: activations staged per warp, the
+// one-shot kernel's bits (lb_gemv.cu gemv_tile_kernel)
+cudaError_t launch_gemv_tile(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
+size_t tile_smem_bytes(int M, int nw, int cpw);
 
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
 int device_error();   // synchronizes

@@ -452,7 +452,9 @@ def test_bias_epilogue_matches_separate_add_and_fp64(layers, name, m):
         assert torch.equal(got, ops.gemv(xc, wq, v) + bc), (name, m, v)
         rms = np.sqrt(np.mean(y64 ** 2))
         err = np.abs(got.double().cpu().numpy() - y64).max() / rms
-        assert err <= NORM_BOUND, (name, m, v, err)
+        # the bias add rounds to fp16 once more: half an ulp at the largest output on top of the GEMV bar
+        extra = 0.5 * float(np.spacing(np.float16(np.abs(y64).max()))) / rms
+        assert err <= NORM_BOUND + extra, (name, m, v, err, extra)
     lin = ops.linear(xc, wq, bias=bc)
     assert torch.equal(lin, ops.linear(xc, wq) + bc)
 
