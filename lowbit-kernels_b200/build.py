@@ -31,8 +31,65 @@ def nvcc():
     return exe
 
 
+FASTCALL_SRC = CSRC / "lb_pyfast.c"
+FASTCALL_OUT = ROOT / "lowbit" / "_fastcall.so"
+
+
+TORCHCALL_SRC = CSRC / "lb_torchcall.cpp"
+TORCHCALL_OUT = ROOT / "lowbit" / "_torchcall.so"
+
+
 def sources():
     return sorted(CSRC.glob("*.cu"))
+
+
+def build_torchcall(force=False, verbose=False):
+    """The CPython extension lowbit/_torchcall.so (ops.gemv's decode path with its tensor checks in C++), compiled
+    against torch's headers and linked to torch's libraries and, with an $ORIGIN run path, to liblowbit_b200.so."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension
+    deps = [TORCHCALL_SRC, OUT] + sorted(INCLUDE.glob("*.h"))
+    if not force and not stale(TORCHCALL_OUT, deps):
+        return TORCHCALL_OUT
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("a C++ compiler is needed for lowbit/_torchcall.so")
+    torch_lib = pathlib.Path(torch.__file__).resolve().parent / "lib"
+    abi = int(torch.compiled_with_cxx11_abi())
+    incs = [f"-I{p}" for p in cpp_extension.include_paths(device_type="cuda")]
+    cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", sysconfig.get_paths()["include"], "-I", str(INCLUDE), *incs, str(TORCHCALL_SRC),
+           "-L", str(OUT.parent), "-l:" + OUT.name, "-L", str(torch_lib), "-lc10", "-lc10_cuda", "-ltorch",
+           "-ltorch_cpu", "-ltorch_python", f"-Wl,-rpath,$ORIGIN:{torch_lib}", "-o", str(TORCHCALL_OUT)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("building lowbit/_torchcall.so failed")
+    return TORCHCALL_OUT
+
+
+def build_fastcall(force=False, verbose=False):
+    """The CPython extension lowbit/_fastcall.so (the decode call path without ctypes), linked to the library with
+    an $ORIGIN run path so it loads the same liblowbit_b200.so beside it."""
+    import sysconfig
+    deps = [FASTCALL_SRC, OUT] + sorted(INCLUDE.glob("*.h"))
+    if not force and not stale(FASTCALL_OUT, deps):
+        return FASTCALL_OUT
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("a C compiler is needed for lowbit/_fastcall.so")
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], "-I", str(INCLUDE),
+           str(FASTCALL_SRC), "-L", str(OUT.parent), "-l:" + OUT.name, "-Wl,-rpath,$ORIGIN", "-o", str(FASTCALL_OUT)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("building lowbit/_fastcall.so failed")
+    return FASTCALL_OUT
 
 
 def headers():
@@ -84,6 +141,8 @@ def build(force=False, verbose=False, ptxas_verbose=False):
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError("linking liblowbit_b200.so failed")
+    build_fastcall(force, verbose)
+    build_torchcall(force, verbose)
     return OUT
 
 

@@ -190,6 +190,9 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
       // the same tiling through the kernel that stages activations per warp (same bits) where it applies and, from
       // an interleaved B200 comparison over the config-1 shapes, is faster: always at M = 1 (1.0-1.3x), on layers of
       // 4096+ rows at M = 2..8 (up to 1.3x; narrower layers keep the CTA-wide asynchronous staging)
+      if (kernel == 4 && m <= 8 && c.ksplit == 1 && c.rt == 1 &&
+          lb::bulk_smem_bytes((int)m, (int)k, c.warps, c.cpw) <= 200 * 1024)
+        return launched(lb::launch_gemv_bulk(p, c, st), "w4_gemv");
       if (kernel != 3 && m <= 8 && (m == 1 || n >= 4096) && c.ksplit == 1 && c.rt == 1 &&
           lb::tile_smem_bytes((int)m, c.warps, c.cpw) <= 200 * 1024)
         return launched(lb::launch_gemv_tile(p, c, st), "w4_gemv");

@@ -910,6 +910,176 @@ cudaError_t launch_gemv_tile(const GemvParams& p, const OneshotConfig& c, cudaSt
   return cudaErrorInvalidConfiguration;
 }
 
+// Plain decode GEMV, M <= 8, the weights of the CTA's 16-row tile landed in shared memory by one bulk copy. The
+// tile's rows are contiguous in the mma layout (16 x K/2 bytes), so one cp.async.bulk moves them -- issued by one
+// thread before the wait on the previous kernel, completing on an mbarrier -- and no register holds a weight in
+// flight: a CTA needs few registers, several CTAs share an SM, and the next kernel in the stream finds room to
+// start its own copies while this one computes. Scales, activations, arithmetic and the reduction are those of
+// gemv_tile_kernel (and so the bits of gemv_oneshot_kernel at the same tiling).
+__host__ __device__ inline size_t bulk_w_bytes(int K) { return (size_t)16 * (K / 2); }
+size_t bulk_smem_bytes(int M, int K, int nw, int cpw) {
+  return bulk_w_bytes(K) + (size_t)nw * M * (cpw * 256 + 16) + (size_t)nw * 16 * M * 4 + 16;
+}
+
+template <int CPW, bool EARLY, bool M1>
+__global__ void __launch_bounds__(512) gemv_bulk_kernel(GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int NW = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int K = p.K, N = p.N, M = M1 ? 1 : p.M, KC = K >> 7, KG = p.KG, cpg = p.cpg;
+  const int n0 = blockIdx.x * 16, rows = min(16, N - n0);
+  const int row_bytes = K >> 1;
+  const int xrow = CPW * 256 + 16;
+  uint8_t* ws = smem;                                             // [16][K/2] weights (rows past N: never read back)
+  uint8_t* xw = smem + bulk_w_bytes(K) + warp * M * xrow;          // this warp's activations
+  float* red = reinterpret_cast<float*>(smem + bulk_w_bytes(K) + NW * M * xrow);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + NW * 16 * M * 4);
+
+  pdl_launch_dependents();
+  if (!EARLY) pdl_wait();
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+    const uint32_t bytes = (uint32_t)rows * (uint32_t)row_bytes;   // a multiple of 64
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_copy_g2s(ws, reinterpret_cast<const uint8_t*>(p.w) + (size_t)n0 * row_bytes, bytes, bar);
+  }
+  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);
+  const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s) + (size_t)ra * KG;
+  const uint16_t* sb = reinterpret_cast<const uint16_t*>(p.s) + (size_t)rb * KG;
+  uint16_t ssa[CPW], ssb[CPW];
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = warp + NW * i;
+    if (c < KC) {
+      const int grp = cpg == 1 ? c : c / cpg;
+      ssa[i] = ldg_u16(sa + grp);
+      ssb[i] = ldg_u16(sb + grp);
+    }
+  }
+  __syncthreads();   // the barrier is initialized before anyone waits on it
+  if (EARLY) pdl_wait_after_loads(p.wait_guard);
+
+  constexpr int PR = M1 ? (CPW / 2 > 0 ? CPW / 2 : 1) : 4;
+  {   // activations of this warp's chunks, as in gemv_tile_kernel
+    const uint8_t* xg = reinterpret_cast<const uint8_t*>(p.x);
+    const int total = M * CPW * 16;
+    for (int base = 0; base < total; base += 32 * PR) {
+      uint4 v[PR];
+      int off[PR];
+#pragma unroll
+      for (int r = 0; r < PR; ++r) {
+        const int e = base + 32 * r + lane;
+        const int m = M1 ? 0 : e / (CPW * 16), rr = M1 ? e : e - m * (CPW * 16), i = rr >> 4, j = rr & 15;
+        const int c = warp + NW * i;
+        off[r] = -1;
+        if (e < total && c < KC) {
+          v[r] = ldg_cg_u4(xg + (size_t)m * K * 2 + (size_t)c * 256 + j * 16);
+          off[r] = m * xrow + i * 256 + j * 16;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < PR; ++r)
+        if (off[r] >= 0) *reinterpret_cast<uint4*>(xw + off[r]) = v[r];
+    }
+  }
+  // the weights have landed (bounded wait: a copy that never completes records kErrBarrierTimeout and the outputs
+  // are undefined, instead of a hang)
+  {
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, 0)) {
+      if (++spins > kSpinLimit) {
+        if (lane == 0) atomicExch(&g_device_status, kErrBarrierTimeout);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+
+  const uint32_t xaddr = smem_u32(xw + min(lane & 7, M - 1) * xrow + (lane >> 3) * 16);
+  const uint8_t* wra = ws + g * row_bytes + t * 16;
+  const uint8_t* wrb = ws + (g + 8) * row_bytes + t * 16;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = warp + NW * i;
+    if (c < KC) {
+      const uint4 qa = *reinterpret_cast<const uint4*>(wra + c * 64);
+      const uint4 qb = *reinterpret_cast<const uint4*>(wrb + c * 64);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        uint32_t xb[4];
+        ldsm_x4(xb, xaddr + i * 256 + qd * 64);
+        const uint32_t w0 = (&qa.x)[qd], w1 = (&qb.x)[qd];
+        uint32_t f[8];
+        f[0] = q_pair_lo(w0); f[1] = q_pair_lo(w1); f[2] = q_pair_hi(w0); f[3] = q_pair_hi(w1);
+        f[4] = q_pair_lo(w0 >> 8); f[5] = q_pair_lo(w1 >> 8); f[6] = q_pair_hi(w0 >> 8); f[7] = q_pair_hi(w1 >> 8);
+        mma16816(d, f[0], f[1], f[2], f[3], xb[0], xb[1]);
+        mma16816(d, f[4], f[5], f[6], f[7], xb[2], xb[3]);
+      }
+      const float s0 = h2f_bits(ssa[i]), s1 = h2f_bits(ssb[i]);
+      acc[0] = fmaf(s0, d[0], acc[0]);
+      acc[2] = fmaf(s1, d[2], acc[2]);
+      if (!M1) {
+        acc[1] = fmaf(s0, d[1], acc[1]);
+        acc[3] = fmaf(s1, d[3], acc[3]);
+      }
+    }
+  }
+  const int MS = 16 * M;
+  if (M1) {
+    if (t == 0) {
+      red[warp * 16 + g] = acc[0];
+      red[warp * 16 + g + 8] = acc[2];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = 2 * t + (i & 1);
+      if (m < M) red[warp * MS + (g + (i >= 2 ? 8 : 0)) * M + m] = acc[i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < MS; e += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < NW; ++w) v += red[w * MS + e];
+    const int row = M1 ? e : e / M, m = M1 ? 0 : e - row * M;
+    if (row < rows) p.y[(size_t)m * N + n0 + row] = out_half(v, p.bias, n0 + row);
+  }
+}
+
+template <int CPW, bool M1>
+static cudaError_t launch_bulk_t(const GemvParams& p, int nw, bool pdl, cudaStream_t st) {
+  auto kern = (p.flags & kFlagEarlyWeights) ? gemv_bulk_kernel<CPW, true, M1> : gemv_bulk_kernel<CPW, false, M1>;
+  const size_t smem = bulk_smem_bytes(p.M, p.K, nw, CPW);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + 15) / 16, 1, 1);
+  cfg.blockDim = dim3(nw * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+cudaError_t launch_gemv_bulk(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
+  if (p.M < 1 || p.M > 8 || c.ksplit != 1 || c.rt != 1 || p.pro || p.epi) return cudaErrorInvalidConfiguration;
+  const bool m1 = p.M == 1;
+#define LB_BULK(CPW_) \
+  if (c.cpw == CPW_) return m1 ? launch_bulk_t<CPW_, true>(p, c.warps, c.pdl, st) : launch_bulk_t<CPW_, false>(p, c.warps, c.pdl, st);
+  LB_BULK(2) LB_BULK(4) LB_BULK(8)
+#undef LB_BULK
+  return cudaErrorInvalidConfiguration;
+}
+
 template <int MT, int RT, int CPW, int PRO = 0, int EPI = 0>
 static cudaError_t launch_oneshot_t(const GemvParams& p, const OneshotConfig& c, cudaStream_t st) {
   auto kern = (p.flags & kFlagEarlyWeights) ? gemv_oneshot_kernel<MT, RT, CPW, true, PRO, EPI>

@@ -76,6 +76,9 @@ size_t oneshot_smem_bytes(int M, int K, int nsplit, int nw, int rt);
 // one-shot kernel's bits (lb_gemv.cu gemv_tile_kernel)
 cudaError_t launch_gemv_tile(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
 size_t tile_smem_bytes(int M, int nw, int cpw);
+// the same with the tile's weights landed in shared memory by one bulk copy (lb_gemv.cu gemv_bulk_kernel)
+cudaError_t launch_gemv_bulk(const GemvParams& p, const OneshotConfig& c, cudaStream_t st);
+size_t bulk_smem_bytes(int M, int K, int nw, int cpw);
 
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
 int device_error();   // synchronizes

@@ -111,46 +111,87 @@ MAX_ROWS = {1: 8, 2: 8, 3: 8, 4: 8, 5: 64, 6: 8}
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_raw_device = getattr(torch._C, "_cuda_getDevice", None)
+_F16 = torch.float16
+_fast = None   # the _fastcall extension module, or False where it was not built (ctypes carries every call then)
+_tc = None     # the _torchcall extension module (tensor checks in C++), or False where it was not built
 
 
 def _current_stream(dev):
     return _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream(dev).cuda_stream
 
 
+def _fastcall():
+    global _fast
+    if _fast is None:
+        try:
+            from . import _fastcall as fc
+            ext()   # the library itself, loaded and checked by the ctypes binding (the extension links the same file)
+            _fast = fc
+        except ImportError:
+            _fast = False
+    return _fast
+
+
+def _torchcall():
+    global _tc
+    if _tc is None:
+        try:
+            from . import _torchcall as tc
+            ext()   # the library itself, loaded and checked by the ctypes binding (the extension links the same file)
+            _tc = tc
+        except ImportError:
+            _tc = False
+    return _tc
+
+
 def _gemv_fast(x, wq, version, out, bias=None):
     """The common decode call with the weight's validated launch arguments cached: cheap checks on x, out and bias,
-    one C call. None when anything is unusual -- the checked path below then handles it (and raises its errors)."""
+    one C call -- through the _torchcall extension (the checks in C++) when it was built, else the checks here and
+    the _fastcall extension or ctypes. None when anything is unusual: the checked path below then handles it (and
+    raises its errors)."""
     args = wq.launch_args(version)
     if args is None:
         return None
+    tc = _tc if _tc is not None else _torchcall()
+    if tc:
+        return tc.gemv(x, args[0], args[1], args[2], wq.n, wq.k, wq.group, version, out, bias)
+    if type(x) is not torch.Tensor or x.dtype is not _F16 or x.dim() != 2:
+        return None
     w_ptr, s_ptr, dev = args
-    if bias is not None and (type(bias) is not torch.Tensor or bias.dtype != torch.float16 or bias.dim() != 1
+    m, kx = x.shape
+    if (kx != wq.k or m == 0 or x.get_device() != dev or not x.is_contiguous()
+            or (_raw_device() if _raw_device is not None else torch.cuda.current_device()) != dev):
+        return None
+    if bias is not None and (type(bias) is not torch.Tensor or bias.dtype is not _F16 or bias.dim() != 1
                              or bias.shape[0] != wq.n or bias.get_device() != dev or not bias.is_contiguous()):
         return None
-    if (type(x) is not torch.Tensor or x.dtype != torch.float16 or x.dim() != 2 or x.shape[1] != wq.k
-            or x.shape[0] == 0 or x.get_device() != dev or not x.is_contiguous()
-            or torch.cuda.current_device() != dev):
-        return None
-    m, n = x.shape[0], wq.n
+    n = wq.n
     if out is None:
-        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
-    elif (out.dtype == torch.float16 and out.dim() == 2 and out.shape[0] == m and out.shape[1] == n
-          and out.get_device() == dev and out.is_contiguous()):
+        y = torch.empty((m, n), dtype=_F16, device=x.device)
+    elif (type(out) is torch.Tensor and out.dtype is _F16 and out.dim() == 2 and out.shape[0] == m
+          and out.shape[1] == n and out.get_device() == dev and out.is_contiguous()):
         y = out
     else:
         return None
-    e = ext()
-    if bias is not None:
-        rc = e.lib.lb_w4_linear(x.data_ptr(), w_ptr, s_ptr, bias.data_ptr(), y.data_ptr(), m, n, wq.k, wq.group,
-                                version, _current_stream(dev))
-    elif version == 6:
-        rc = e.lib.lb_w4_gemv(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, wq.k, wq.group, 6, 0,
-                              _current_stream(dev))
+    fc = _fast if _fast is not None else _fastcall()
+    st = _current_stream(dev)
+    if fc:
+        if bias is None:
+            rc = fc.gemv(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, kx, wq.group, version, st)
+        else:
+            rc = fc.linear(x.data_ptr(), w_ptr, s_ptr, bias.data_ptr(), y.data_ptr(), m, n, kx, wq.group, version, st)
     else:
-        rc = e.lib.lb_w4_gemm_tc(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, wq.k, wq.group, 0,
-                                 _current_stream(dev))
+        lib = ext().lib
+        if bias is not None:
+            rc = lib.lb_w4_linear(x.data_ptr(), w_ptr, s_ptr, bias.data_ptr(), y.data_ptr(), m, n, kx, wq.group,
+                                  version, st)
+        elif version == 6:
+            rc = lib.lb_w4_gemv(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, kx, wq.group, 6, 0, st)
+        else:
+            rc = lib.lb_w4_gemm_tc(x.data_ptr(), w_ptr, s_ptr, y.data_ptr(), m, n, kx, wq.group, 0, st)
     if rc:
-        e._raise(rc)
+        ext()._raise(rc)
     return y
 
 

@@ -132,3 +132,17 @@ def test_linear_rejections(lib):
     assert lib.lb_w4_linear(A, A, A, A, A, 65, 64, 256, 128, 5, None) == 1
     assert b"1..64 rows" in lib.lb_last_error()
     assert lib.lb_w4_linear(A, A, A, None, A, 2, 64, 256, 128, 7, None) == 1
+
+
+def test_fastcall_extension_calls_the_same_library(lib):
+    """lowbit/_fastcall.so (the decode call path without ctypes) reaches the same loaded library: its refusals
+    come back with the C ABI's status codes and set the same lb_last_error() message."""
+    from lowbit import _fastcall
+    A = FakePtr.A
+    assert _fastcall.gemv(A, A, A, A, 1, 64, 256, 0, 6, None) == 1
+    assert b"group size must be positive" in lib.lb_last_error()
+    assert _fastcall.gemv(A, A, A, A, 65, 64, 256, 128, 5, None) == 1
+    assert b"1..64 rows" in lib.lb_last_error()
+    assert _fastcall.linear(A, A, A, FakePtr.U, A, 1, 64, 256, 128, 6, None) == 2
+    with pytest.raises(TypeError):
+        _fastcall.gemv(A, A)

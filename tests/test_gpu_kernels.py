@@ -160,12 +160,13 @@ def test_v6_gemv_parity(layers, name, m):
     check_output(y, ref_y(x, packed, scales, 128), f"v6 {name} M={m}")
 
 
-@pytest.mark.parametrize("kernel", [0, 1, 2])
+@pytest.mark.parametrize("kernel", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("name", ["0.5b.kv", "1.5b.up", "3b.down", "odd_n", "tiny", "k128"])
 @pytest.mark.parametrize("m", [1, 3, 7, 8, 16, 24])
 def test_every_gemv_kernel(layers, kernel, name, m):
     """Each kernel forced through the option against the oracle, whatever the dispatch would pick: automatic (0),
-    the copy-ring GEMV (1) and the tcgen05 GEMM (2)."""
+    the copy-ring GEMV (1), the tcgen05 GEMM (2), the one-shot GEMV with CTA-wide staging (3) and the bulk-copy
+    GEMV (4; 3 and 4 up to 8 rows, the automatic choice beyond)."""
     k, n, w, packed, scales, wq = layers[name]
     x = x_for(m, k, k + n + 5 * m)
     e = ops.ext()
