@@ -532,7 +532,8 @@ __global__ void __launch_bounds__(512) gemv_oneshot_kernel(GemvParams p) {
   };
   auto cta_sum = [&](int e) {
     float v = 0.f;
-    for (int w = 0; w < NW; ++w) v += red[w * kTile + e];
+#pragma unroll 8
+    for (int w = 0; w < NW; ++w) v += red[w * kTile + e];   // the loads issue together; the adds keep their order
     return v;
   };
   // the finished tile: one CTA's warps summed (nsplit == 1), or, with K split over a cluster, each rank's sum
@@ -871,7 +872,8 @@ __global__ void __launch_bounds__(512) gemv_tile_kernel(GemvParams p) {
   __syncthreads();
   for (int e = threadIdx.x; e < MS; e += blockDim.x) {   // 16 M outputs; a one-warp CTA loops at M > 2
     float v = 0.f;
-    for (int w = 0; w < NW; ++w) v += red[w * MS + e];
+#pragma unroll 8
+    for (int w = 0; w < NW; ++w) v += red[w * MS + e];   // the loads issue together; the adds keep their order
     const int row = M1 ? e : e / M, m = M1 ? 0 : e - row * M;
     if (n0 + row < N) p.y[(size_t)m * N + n0 + row] = out_half(v, p.bias, n0 + row);
   }
@@ -1043,7 +1045,8 @@ __global__ void __launch_bounds__(512) gemv_bulk_kernel(GemvParams p) {
   __syncthreads();
   for (int e = threadIdx.x; e < MS; e += blockDim.x) {
     float v = 0.f;
-    for (int w = 0; w < NW; ++w) v += red[w * MS + e];
+#pragma unroll 8
+    for (int w = 0; w < NW; ++w) v += red[w * MS + e];   // the loads issue together; the adds keep their order
     const int row = M1 ? e : e / M, m = M1 ? 0 : e - row * M;
     if (row < rows) p.y[(size_t)m * N + n0 + row] = out_half(v, p.bias, n0 + row);
   }
