@@ -605,7 +605,7 @@ def run_ours(args, rank, world, local):
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "gemv_oneshot_kernel (M=1 decode GEMV)",
+            "bound": "hbm", "kernel": "gemv_tile_kernel (M=1 decode GEMV)",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "algorithmic_bytes_per_launch": round(step_bytes / launches_per_step),
             "frac": round(achieved / peak, 4), "peak_source": peak_src,
