@@ -84,6 +84,10 @@ class W4Weight:
     def launch_args(self, version):
         """(packed pointer, scales pointer, device index) of the layout `version` reads, or None if that layout is
         not kept or not launchable; validated once per tensor object (replacing a layout tensor revalidates)."""
+        if version == 5 or version == 6:   # the decode path: one attribute holds the mma copy's arguments
+            hit = self.__dict__.get("_mma_launch")
+            if hit is not None and hit[0] is self.packed_mma and hit[1] is self.scales:
+                return hit[2]
         w, s = getattr(self, NEEDS[version]), self.scales
         cache = self.__dict__.setdefault("_launch", {})
         hit = cache.get(version)
@@ -97,6 +101,8 @@ class W4Weight:
                 and tuple(s.shape) == (self.n, self.k // self.group)):
             args = (w.data_ptr(), s.data_ptr(), w.get_device())
         cache[version] = (w, s, args)
+        if version == 5 or version == 6:
+            self.__dict__["_mma_launch"] = (w, s, args)
         return args
 
 
@@ -219,6 +225,9 @@ def gemv(x, wq, version=4, rows_per_warp=0, out=None, bias=None):
     return ext().w4_gemv(x.contiguous(), w, wq.scales, wq.group, version, rows_per_warp, out=out)
 
 
+_GEMV = gemv   # linear()'s shortcut applies only while ops.gemv is this function (tests may replace it)
+
+
 def quantize_w4_gpu(w, group=128, clip_grid=None, rows_per_pass=2048):
     """Same format and, with clip_grid=None, the same bits as quant.quantize_w4, computed by the quantize kernel.
     clip_grid, e.g. (1.0, 0.95, ..., 0.75): per group, try scale = a * amax / 7 for each a and keep the first one
@@ -312,6 +321,14 @@ def linear(x, wq, max_gemv_rows=8, version=0, out=None, bias=None):
     to the result (in the INT4 kernels' epilogue; after the cuBLAS product on the prefill path) with the roundings
     of adding it to the fp16 output."""
     m = x.shape[0]
+    if version == 0 and m and type(wq) is W4Weight and wq.packed_mma is not None and gemv is _GEMV:
+        # the decode call: the rule of auto_version inline, straight to the cached launch (anything unusual falls
+        # through to the general path below)
+        v = 6 if m <= AUTO_GEMV_ROWS else 5 if m <= (AUTO_V5_WIDE_ROWS if wq.n >= AUTO_WIDE_N else AUTO_V5_ROWS) else 0
+        if v:
+            y = _gemv_fast(x, wq, v, out, bias)
+            if y is not None:
+                return y
     if m == 0:
         return x.new_empty(0, wq.n) if out is None else out
     if version == 0:

@@ -128,3 +128,71 @@ def test_row_parallel_sum_and_vocab_argmax_over_gloo():
     for r in range(world):
         assert results[f"mlp{r}"] < 1e-5, results[f"mlp{r}"]
         assert results[f"tok{r}"] == 10
+
+
+def _attn_worker(rank, world, port, results):
+    """One rank of a tensor-parallel attention block at the Qwen2.5-7B head layout (28 query heads, 4 kv heads, so at
+    8 ranks each kv head is held by two ranks that split its 7 query heads 3 + 4), small dims, fp64: the rank's
+    q|k|v rows, grouped attention of its local heads over a cache, its o-projection partial, summed over ranks."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        nh, nkv, hd, inter, ctx = 28, 4, 16, 1024, 6
+        h = nh * hd
+        g = torch.Generator().manual_seed(21)
+        w = {"q": torch.randn(nh * hd, h, generator=g, dtype=torch.float64) * 0.05,
+             "k": torch.randn(nkv * hd, h, generator=g, dtype=torch.float64) * 0.05,
+             "v": torch.randn(nkv * hd, h, generator=g, dtype=torch.float64) * 0.05,
+             "o": torch.randn(h, nh * hd, generator=g, dtype=torch.float64) * 0.05,
+             "gate": torch.randn(inter, h, generator=g, dtype=torch.float64),
+             "up": torch.randn(inter, h, generator=g, dtype=torch.float64),
+             "down": torch.randn(h, inter, generator=g, dtype=torch.float64),
+             "q_b": torch.randn(nh * hd, generator=g, dtype=torch.float64) * 0.1,
+             "k_b": torch.randn(nkv * hd, generator=g, dtype=torch.float64) * 0.1,
+             "v_b": torch.randn(nkv * hd, generator=g, dtype=torch.float64) * 0.1}
+        x = torch.randn(h, generator=g, dtype=torch.float64)
+        kcache = torch.randn(nkv, ctx, hd, generator=g, dtype=torch.float64)
+        vcache = torch.randn(nkv, ctx, hd, generator=g, dtype=torch.float64)
+
+        def attend(q, k_new, v_new, kc, vc, n_q, n_kv):
+            grp = n_q // n_kv
+            out = []
+            for i in range(n_q):
+                j = i // grp                                   # one uniform query group per kv head
+                K = torch.cat([kc[j], k_new[j][None]])
+                V = torch.cat([vc[j], v_new[j][None]])
+                a = torch.softmax(K @ q[i] / hd ** 0.5, 0)
+                out.append(a @ V)
+            return torch.cat(out)
+
+        # unsharded reference
+        qf = (w["q"] @ x + w["q_b"]).view(nh, hd)
+        kf = (w["k"] @ x + w["k_b"]).view(nkv, hd)
+        vf = (w["v"] @ x + w["v_b"]).view(nkv, hd)
+        want = w["o"] @ attend(qf, kf, vf, kcache, vcache, nh, nkv)
+
+        p = tp.plan(nh, nkv, hd, inter, 1000, world, rank)
+        sh = tp.shard_layer(w, p)
+        (q0, q1), (k0, k1) = p["q_heads"], p["kv_heads"]
+        nq, nk = q1 - q0, k1 - k0
+        qkv = sh["qkv"] @ x + sh["bias"]
+        q = qkv[:nq * hd].view(nq, hd)
+        k_new = qkv[nq * hd:(nq + nk) * hd].view(nk, hd)
+        v_new = qkv[(nq + nk) * hd:].view(nk, hd)
+        y = sh["o"] @ attend(q, k_new, v_new, kcache[k0:k1], vcache[k0:k1], nq, nk)
+        dist.all_reduce(y)
+        results[f"err{rank}"] = float((y - want).abs().max() / want.abs().max())
+        results[f"heads{rank}"] = (nq, nk)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_uneven_tp8_attention_over_gloo():
+    """Qwen2.5-7B's head layout split over 8 ranks (kv heads replicated, query groups 3 + 4) reproduces the
+    unsharded attention block: shard plan, fused q|k|v rows and bias, local grouping, row-parallel o and the sum."""
+    world = 8
+    results = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_attn_worker, args=(world, _free_port(), results), nprocs=world, start_method="spawn")
+    assert sorted(results[f"heads{r}"] for r in range(world)) == [(3, 1)] * 4 + [(4, 1)] * 4
+    for r in range(world):
+        assert results[f"err{r}"] < 1e-12, results[f"err{r}"]
