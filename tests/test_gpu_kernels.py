@@ -311,7 +311,7 @@ def test_cached_launch_path_matches_the_checked_path():
         else:
             want = e.w4_gemm_tc(x, wq.packed_mma, wq.scales, wq.group)
         assert torch.equal(ops.gemv(x, wq, v), want)
-        assert v in wq._launch and wq._launch[v][2] is not None
+        assert wq.launch_args(v) is not None
         out = torch.empty(m, 2048, device="cuda").half()
         assert ops.gemv(x, wq, v, out=out) is out and torch.equal(out, want)
     xs = torch.randn(1536, 2).half().cuda().t()[:1]            # not contiguous
@@ -320,7 +320,7 @@ def test_cached_launch_path_matches_the_checked_path():
     before = ops.gemv(x, wq, 6)
     wq.packed_mma = wq.packed_mma.clone()
     assert torch.equal(ops.gemv(x, wq, 6), before)
-    assert wq._launch[6][0] is wq.packed_mma
+    assert wq.launch_args(6)[0] == wq.packed_mma.data_ptr()
 
 
 def test_fixed_version_past_its_limit_falls_back():
