@@ -53,8 +53,12 @@ typedef enum lb_option {
   LB_OPT_GEMV_DEPTH = 4,    /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
   LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 forces the persistent copy-ring GEMV, 2 the tcgen05
                                GEMM (any M <= 64), 3 the one-shot GEMV with activations staged per CTA (the
-                               automatic choice at M <= 8 stages them per warp, with the same bits) */
-  LB_OPT_GEMV_ROWTILES = 6  /* 0 (default): automatic; 1 or 2 forces the one-shot GEMV's 16-row tiles per CTA */
+                               automatic choice at M <= 8 stages them per warp, with the same bits), 4 the
+                               M <= 8 GEMV with each weight tile landed in shared memory by one bulk copy, 5 the
+                               skinny GEMM on mma.sync tiles fed by tensor copies (any M <= 64; the automatic
+                               choice above 16 rows) */
+  LB_OPT_GEMV_ROWTILES = 6  /* 0 (default): automatic; 1 or 2 forces the one-shot GEMV's 16-row tiles per CTA, and
+                               the skinny GEMM's 16-row tiles per warp */
 } lb_option;
 
 /* ABI version of this header; bumped on any signature change. */

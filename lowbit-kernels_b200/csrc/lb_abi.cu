@@ -178,7 +178,16 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                    (int)(group / 128)};
   p.bias = static_cast<const __half*>(bias);
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
-  if (kernel == 2 || (kernel == 0 && m > 16)) {
+  // the skinny GEMM above 16 rows, and from 9 rows on layers of 8M+ weights or K < 512 (there, measured on B200,
+  // 1.2-2.4x faster than the one-shot GEMV's 16-row CTAs, which each re-read every activation row)
+  if (kernel == 5 || (kernel == 0 && (m > 16 || (m > 8 && (n * k >= (int64_t)1 << 23 || k < 512))))) {
+    // mma.sync tiles fed by tensor copies: CTAs of 64-128 weight rows sharing each activation chunk, clusters
+    // splitting K
+    const lb::MmaConfig c = lb::gemm_mma_config((int)m, (int)n, (int)k, (int)group,
+                                                g_opt[LB_OPT_GEMV_KSPLIT].load(), g_opt[LB_OPT_GEMV_ROWTILES].load());
+    if (c.splits > 0) return launched(lb::launch_gemm_mma(p, c, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm");
+  }
+  if (kernel == 2) {
     // tcgen05: per 128-row tile a cluster of CTAs splitting K, tensor-memory accumulators
     const int splits = lb::gemm_tc05_splits((int)m, (int)n, (int)k, (int)group, g_opt[LB_OPT_GEMV_KSPLIT].load());
     if (splits > 0)
@@ -236,6 +245,7 @@ const char* lb_last_error(void) { return g_err; }
 int lb_device_error(void) {
   int a = lb::device_error();
   if (!a) a = lb::gemm_tc_device_error();
+  if (!a) a = lb::gemm_mma_device_error();
   if (!a) a = lb::allreduce_device_error();
   return a ? a : lb::decode_device_error();
 }
@@ -243,6 +253,7 @@ int lb_device_error(void) {
 void lb_clear_device_error(void) {
   lb::clear_device_error();
   lb::gemm_tc_clear_device_error();
+  lb::gemm_mma_clear_device_error();
   lb::allreduce_clear_device_error();
   lb::decode_clear_device_error();
 }

@@ -128,4 +128,17 @@ cudaError_t launch_gemm_tc05(const GemvParams& p, int splits, bool pdl, cudaStre
 int gemm_tc_device_error();   // synchronizes
 void gemm_tc_clear_device_error();
 
+// skinny GEMM on mma.sync tiles fed by tensor copies (lb_gemm_mma.cu), M <= 64 (exact per-group products up to 16
+// rows, fp16-rounded weights above): CTAs of 64 rt weight rows, `splits` of them per cluster splitting K.
+// gemm_mma_config picks both for a shape on the current device (forced > 0: that split / row-tile count), splits 0
+// if the shape does not fit the kernel.
+struct MmaConfig {
+  int splits;
+  int rt;
+};
+MmaConfig gemm_mma_config(int M, int N, int K, int G, int forced_splits, int forced_rt);
+cudaError_t launch_gemm_mma(const GemvParams& p, const MmaConfig& c, bool pdl, cudaStream_t st);
+int gemm_mma_device_error();   // synchronizes
+void gemm_mma_clear_device_error();
+
 }  // namespace lb

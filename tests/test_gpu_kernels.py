@@ -160,13 +160,14 @@ def test_v6_gemv_parity(layers, name, m):
     check_output(y, ref_y(x, packed, scales, 128), f"v6 {name} M={m}")
 
 
-@pytest.mark.parametrize("kernel", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("kernel", [0, 1, 2, 3, 4, 5])
 @pytest.mark.parametrize("name", ["0.5b.kv", "1.5b.up", "3b.down", "odd_n", "tiny", "k128"])
 @pytest.mark.parametrize("m", [1, 3, 7, 8, 16, 24])
 def test_every_gemv_kernel(layers, kernel, name, m):
     """Each kernel forced through the option against the oracle, whatever the dispatch would pick: automatic (0),
-    the copy-ring GEMV (1), the tcgen05 GEMM (2), the one-shot GEMV with CTA-wide staging (3) and the bulk-copy
-    GEMV (4; 3 and 4 up to 8 rows, the automatic choice beyond)."""
+    the copy-ring GEMV (1), the tcgen05 GEMM (2), the one-shot GEMV with CTA-wide staging (3), the bulk-copy
+    GEMV (4; 3 and 4 up to 8 rows, the automatic choice beyond) and the skinny mma.sync GEMM (5; exact per-group
+    products up to 16 rows)."""
     k, n, w, packed, scales, wq = layers[name]
     x = x_for(m, k, k + n + 5 * m)
     e = ops.ext()
@@ -176,7 +177,7 @@ def test_every_gemv_kernel(layers, kernel, name, m):
     finally:
         e.set_option("gemv_kernel", prev)
     y64 = ref_y(x, packed, scales, 128)
-    if kernel == 2 or (kernel == 0 and m > 16):
+    if kernel == 2 or (kernel in (0, 5) and m > 16):
         check_gemm_output(y, y64, x, packed, scales, 128, f"kernel {kernel} {name} M={m}")
     else:
         check_output(y, y64, f"kernel {kernel} {name} M={m}")
@@ -214,6 +215,75 @@ def test_tcgen05_gemm_parity(layers, name, m):
     finally:
         e.set_option("gemv_kernel", prev)
     check_gemm_output(y, ref_y(x, packed, scales, 128), x, packed, scales, 128, f"tcgen05 {name} M={m}")
+
+
+@pytest.mark.parametrize("name", [s[0] for s in SHAPES + EDGE])
+@pytest.mark.parametrize("m", [1, 9, 16, 17, 24, 32, 33, 40, 48, 49, 64])
+def test_mma_gemm_parity(layers, name, m):
+    """The skinny mma.sync GEMM at every activation-tile width (16 / 32 / 48 / 64 rows), forced at every M: exact
+    per-group products up to 16 rows (the GEMV's bar), fp16-rounded weights above (the cuBLAS bar)."""
+    k, n, w, packed, scales, wq = layers[name]
+    x = x_for(m, k, k + n + 11 * m)
+    e = ops.ext()
+    prev = e.set_option("gemv_kernel", 5)
+    try:
+        y = ops.gemv(x.cuda(), wq, 5)
+    finally:
+        e.set_option("gemv_kernel", prev)
+    y64 = ref_y(x, packed, scales, 128)
+    if m > 16:
+        check_gemm_output(y, y64, x, packed, scales, 128, f"mma gemm {name} M={m}")
+    else:
+        check_output(y, y64, f"mma gemm {name} M={m}")
+
+
+@pytest.mark.parametrize("ksplit", [1, 2, 3, 7, 8])
+@pytest.mark.parametrize("rt", [1, 2])
+@pytest.mark.parametrize("m", [12, 40])
+def test_mma_gemm_forced_splits_and_row_tiles(ksplit, rt, m):
+    """Every cluster size and row-tile count of the skinny GEMM gives the same result within its bar (the split
+    only changes the fp32 summation order)."""
+    e = ops.ext()
+    k, n = 4864, 1000
+    packed, scales = quant.quantize_w4(seeded(n, k, 5), 128)
+    wq = ops.W4Weight(packed, scales, 128, ("mma",))
+    x = x_for(m, k, 5)
+    prev = {o: e.set_option(o, v) for o, v in (("gemv_kernel", 5), ("gemv_ksplit", ksplit), ("gemv_rowtiles", rt))}
+    try:
+        y = ops.gemv(x.cuda(), wq, 5)
+    finally:
+        for o, v in prev.items():
+            e.set_option(o, v)
+    y64 = ref_y(x, packed, scales, 128)
+    if m > 16:
+        check_gemm_output(y, y64, x, packed, scales, 128, f"ksplit={ksplit} rt={rt} M={m}")
+    else:
+        check_output(y, y64, f"ksplit={ksplit} rt={rt} M={m}")
+
+
+def test_mma_gemm_group_256_and_bias(layers):
+    """Two chunks per scale group, and the bias epilogue, through the skinny GEMM."""
+    k, n = 2048, 768
+    w = seeded(n, k, 9)
+    packed, scales = quant.quantize_w4(w, 256)
+    wq = ops.W4Weight(packed, scales, 256, ("mma",))
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(4)) * 0.1).half()
+    for m in (12, 37, 64):
+        x = x_for(m, k, 21 + m)
+        y64 = ref_y(x, packed, scales, 256)
+        e = ops.ext()
+        prev = e.set_option("gemv_kernel", 5)
+        try:
+            y = ops.gemv(x.cuda(), wq, 5)
+            yb = ops.gemv(x.cuda(), wq, 5, bias=bias.cuda())
+        finally:
+            e.set_option("gemv_kernel", prev)
+        if m > 16:
+            check_gemm_output(y, y64, x, packed, scales, 256, f"G=256 M={m}")
+        else:
+            check_output(y, y64, f"G=256 M={m}")
+        want = (y.float() + bias.cuda().float()).half()
+        assert torch.equal(yb, want), f"bias M={m}"
 
 
 @pytest.mark.parametrize("name", [s[0] for s in SHAPES + EDGE])
