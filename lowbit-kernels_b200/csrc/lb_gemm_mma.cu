@@ -5,15 +5,14 @@
 // prefill path. At these sizes the work is a stream of 4-bit weights (N K / 2 bytes) against a few activation
 // rows that every weight row needs, so the design keeps each weight byte read from HBM once and each activation
 // byte read from L2 once per CTA:
-//   * a CTA owns 128 RT weight rows (8 warps x RT 16-row tiles) and a contiguous K range; the S CTAs of a column
-//     of the grid form a thread-block cluster that splits K and adds its fp32 partial tiles through distributed
-//     shared memory in a fixed rank order (deterministic, no workspace);
-//   * one thread (warp 0, lane 0) streams the range through a ring of stages, one 128-wide K chunk each: the
-//     CTA's packed weight rows (a 2-D tensor copy of 64-byte rows) and the chunk's activations (two 2-D tensor
-//     copies of 64 k x 8 MT rows, 128-byte swizzle, rows past M read as zeros), completing on the stage's
-//     mbarrier. The weights of the first stages are requested before the wait on the previous kernel in the
-//     stream; later stages are refilled one chunk behind the consumers, once all eight warps released them (no
-//     separate producer warp: 16 warps of two CTAs share an SM within its register file);
+//   * a CTA owns 64 RT weight rows (4 consumer warps x RT 16-row tiles) and a contiguous K range; the S CTAs of a
+//     column of the grid form a thread-block cluster that splits K and adds its fp32 partial tiles through
+//     distributed shared memory in a fixed rank order (deterministic, no workspace). (128-row CTAs of 8 warps
+//     measured slower: narrow layers then need splits that leave each CTA one or two chunks);
+//   * a producer thread streams the range through a ring of stages, one 128-wide K chunk each: the CTA's packed
+//     weight rows (a 2-D tensor copy of 64-byte rows) and the chunk's activations (two 2-D tensor copies of 64 k x
+//     8 MT rows, 128-byte swizzle, rows past M read as zeros), completing on the stage's mbarrier; the weights of
+//     the first stages are requested before the wait on the previous kernel in the stream;
 //   * every consumer warp reads the chunk's activation fragments once per 32 k (ldmatrix, conflict-free through
 //     the swizzle) and uses each for its RT row tiles, so shared-memory traffic per weight is 2 M / (16 RT) bytes;
 //     its weights come from the stage as one 16-byte read per row and chunk, are decoded with the lop3 / f16x2
@@ -39,9 +38,10 @@ __device__ int g_mma_status;   // a bounded wait in this file's kernel gave up; 
 
 namespace {
 
-constexpr int kConsumerWarps = 8;                        // each owns RT 16-row tiles; warp 0 lane 0 also loads
-constexpr int kMmaThreads = kConsumerWarps * 32;
-constexpr int kRingBudget = 96 * 1024;                     // stage ring per CTA: two CTAs fit one SM
+constexpr int kConsumerWarps = 4;                        // each owns RT 16-row tiles
+constexpr int kMmaThreads = (kConsumerWarps + 1) * 32;   // + the producer warp
+constexpr int kRingBudget = 96 * 1024;                     // stage ring per CTA: two CTAs fit one SM (a 64 KB
+                                                           // ring for three measured slower: too shallow)
 constexpr int kMaxStages = 8;
 constexpr int kMaxClusterSplits = 8;
 
@@ -96,9 +96,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
   const int n0 = blockIdx.x * ROWS;
   const int KC = p.K >> 7;
   const int c_begin = (KC * (int)blockIdx.y) / S, nc = (KC * ((int)blockIdx.y + 1)) / S - c_begin;
-  const bool loader = threadIdx.x == 0;
+  const bool producer = warp == kConsumerWarps;
 
-  if (loader) {
+  if (threadIdx.x == 0) {
     for (int s = 0; s < D; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
@@ -117,16 +117,30 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
     tma_load_2d(smem + s * SB, &xmap, (c_begin + i) * 128, 0, &full[s]);
     tma_load_2d(smem + s * SB + XB / 2, &xmap, (c_begin + i) * 128 + 64, 0, &full[s]);
   };
-  const int first = nc < D ? nc : D;
-  if (loader) {
-    tma_prefetch_map(&wmap);
-    tma_prefetch_map(&xmap);
-    const bool early = (p.flags & kFlagEarlyWeights) != 0;
-    if (!early && p.wait_guard) pdl_wait();
-    // the weights of the first stages do not depend on the previous kernel: requested before its wait
-    for (int i = 0; i < first; ++i) load_weights(i, i);
-    if (early && p.wait_guard) pdl_wait();
-    for (int i = 0; i < first; ++i) load_x(i, i);
+  if (producer) {
+    // ------------------------------------------------------------------ producer (one thread)
+    if (lane == 0) {
+      tma_prefetch_map(&wmap);
+      tma_prefetch_map(&xmap);
+      const bool early = (p.flags & kFlagEarlyWeights) != 0;
+      if (!early && p.wait_guard) pdl_wait();
+      const int first = nc < D ? nc : D;
+      // the weights of the first stages do not depend on the previous kernel: requested before its wait
+      for (int i = 0; i < first; ++i) load_weights(i, i);
+      if (early && p.wait_guard) pdl_wait();
+      for (int i = 0; i < first; ++i) load_x(i, i);
+      int issued = first;
+      for (int i = D; i < nc; ++i) {
+        const int s = i % D;
+        if (!wait_bounded(&empty[s], ((i / D) - 1) & 1, &g_mma_status)) break;
+        load_weights(i, s);
+        load_x(i, s);
+        issued = i + 1;
+      }
+      // none of this CTA's copies may still be in flight when it exits
+      for (int i = issued > D ? issued - D : 0; i < issued; ++i) wait_full(&full[i % D], (i / D) & 1);
+    }
+    __syncwarp();
   }
 
   // the CTA's scales, [ROWS][ng] for groups g0 .. g0 + ng - 1, fetched once with every load of a batch in flight
@@ -134,25 +148,26 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
   const int KG = p.KG, cpg = p.cpg, NG = p.ngroups;
   const int g0 = c_begin / cpg, ng = nc > 0 ? (c_begin + nc - 1) / cpg - g0 + 1 : 0;
   uint16_t* sc = reinterpret_cast<uint16_t*>(smem + scales_offset(MT, RT));
-  {
+  constexpr int kCT = kConsumerWarps * 32;
+  if (!producer) {
     const uint16_t* sp = reinterpret_cast<const uint16_t*>(p.s);
     const int total = ROWS * ng;
     constexpr int kBatch = 8;
-    for (int base = threadIdx.x; base < total; base += kMmaThreads * kBatch) {
+    for (int base = threadIdx.x; base < total; base += kCT * kBatch) {
       uint16_t v[kBatch];
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        const int idx = base + kMmaThreads * j, row = idx / ng;
+        const int idx = base + kCT * j, row = idx / ng;
         if (idx < total) v[j] = ldg_u16(sp + (size_t)min(n0 + row, N - 1) * KG + g0 + (idx - row * ng));
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        const int idx = base + kMmaThreads * j, row = idx / ng;
+        const int idx = base + kCT * j, row = idx / ng;
         if (idx < total) sc[row * NG + idx - row * ng] = v[j];
       }
     }
+    named_barrier(1, kCT);
   }
-  __syncthreads();
   // this lane's scales: row g of tile r at sc_lane + 16 r NG, row g + 8 another 8 NG further
   const uint16_t* sc_lane = sc + (16 * RT * warp + g) * NG;
   // ldmatrix: lane L addresses row L & 7 of 8x8 matrix L >> 3 (k piece (L >> 3) of a 32-k block); in a swizzled
@@ -170,26 +185,33 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[r][mt][i] = 0.f;
 
+  // Software-pipelined: the activation fragments of the next 32-k block (at a chunk's last block: the next
+  // chunk's first block and weights, after waiting for its stage) are read before this block's MMAs are issued,
+  // so a single warp per scheduler keeps the tensor pipe fed across the shared-memory latency.
   bool ok = true;
-  for (int i = 0; i < nc; ++i) {
-    const int s = i % D;
-    // the loader refills the stage of chunk i - 1 (with chunk i - 1 + D) once every warp has released it
-    if (loader && i >= 1 && i - 1 + D < nc && ok) {
-      const int sp = (i - 1) % D;
-      ok = wait_bounded(&empty[sp], ((i - 1) / D) & 1, &g_mma_status);
-      if (ok) {
-        load_weights(i - 1 + D, sp);
-        load_x(i - 1 + D, sp);
-      }
-    }
-    if (ok) ok = wait_full(&full[s], (i / D) & 1);
-    const uint32_t xs = ring + s * SB, ws = xs + XB;
-    uint4 qa[RT], qb[RT];
+  const int my_nc = producer ? 0 : nc;
+  uint4 qa[RT], qb[RT];
+  uint32_t xb[2][MT][4];
+  auto load_w = [&](int i, uint4 (&a)[RT], uint4 (&b)[RT]) {
+    const uint32_t ws = ring + (i % D) * SB + XB + wo;
 #pragma unroll
     for (int r = 0; r < RT; ++r) {
-      qa[r] = lds128(ws + wo + r * 1024);
-      qb[r] = lds128(ws + wo + r * 1024 + 512);
+      a[r] = lds128(ws + r * 1024);
+      b[r] = lds128(ws + r * 1024 + 512);
     }
+  };
+  auto load_xb = [&](uint32_t (&dst)[MT][4], int i, int qd) {
+    const uint32_t xq = ring + (i % D) * SB + (uint32_t)(qd >> 1) * (XB / 2) + ((qd & 1) ? xo1 : xo0);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) ldsm_x4(dst[mt], xq + mt * 1024);
+  };
+  if (my_nc > 0) {
+    ok = wait_full(&full[0], 0);
+    load_w(0, qa, qb);
+    load_xb(xb[0], 0, 0);
+  }
+  for (int i = 0; i < my_nc; ++i) {
+    const int s = i % D;
     const int gi = (cpg == 1 ? c_begin + i : (c_begin + i) / cpg) - g0;
     uint32_t s2a[RT], s2b[RT];
     float fa[RT], fb[RT];
@@ -210,12 +232,16 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
 #pragma unroll
           for (int j = 0; j < 4; ++j) d[r][mt][j] = 0.f;
     }
+    uint4 qa_n[RT], qb_n[RT];
 #pragma unroll
     for (int qd = 0; qd < 4; ++qd) {
-      uint32_t xb[MT][4];
-      const uint32_t xq = xs + (uint32_t)(qd >> 1) * (XB / 2) + ((qd & 1) ? xo1 : xo0);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) ldsm_x4(xb[mt], xq + mt * 1024);
+      if (qd < 3) {
+        load_xb(xb[(qd + 1) & 1], i, qd + 1);
+      } else if (i + 1 < my_nc) {
+        if (ok) ok = wait_full(&full[(i + 1) % D], ((i + 1) / D) & 1);
+        load_w(i + 1, qa_n, qb_n);
+        load_xb(xb[0], i + 1, 0);
+      }
       uint32_t f[RT][8];
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
@@ -240,12 +266,12 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             float (&dd)[4] = EXACT ? d[EXACT ? r : 0][EXACT ? mt : 0] : acc[r][mt];
-            mma16816(dd, f[r][4 * h], f[r][4 * h + 1], f[r][4 * h + 2], f[r][4 * h + 3], xb[mt][2 * h],
-                     xb[mt][2 * h + 1]);
+            mma16816(dd, f[r][4 * h], f[r][4 * h + 1], f[r][4 * h + 2], f[r][4 * h + 3], xb[qd & 1][mt][2 * h],
+                     xb[qd & 1][mt][2 * h + 1]);
           }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0) mbar_arrive(&empty[s]);   // every read of stage s is done (the next stage's came after)
     if constexpr (EXACT) {
 #pragma unroll
       for (int r = 0; r < RT; ++r)
@@ -257,25 +283,27 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
           acc[r][mt][3] = fmaf(fb[r], d[r][mt][3], acc[r][mt][3]);
         }
     }
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      qa[r] = qa_n[r];
+      qb[r] = qb_n[r];
+    }
   }
-  // after a wait that gave up, copies may still be in flight: the loader waits (bounded) for the ones it issued
-  if (loader && !ok) {
-    for (int i = 0; i < nc; ++i) wait_full(&full[i % D], (i / D) & 1);
-  }
-
   // the outputs are written in stream order
   if (p.wait_guard) pdl_wait();
   __syncthreads();   // every stage consumed and every copy landed: the ring becomes the partial tile
   float* part = reinterpret_cast<float*>(smem);
+  if (!producer) {
 #pragma unroll
-  for (int r = 0; r < RT; ++r)
+    for (int r = 0; r < RT; ++r)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = 16 * (RT * warp + r) + g + (i >= 2 ? 8 : 0), m = 8 * mt + 2 * t + (i & 1);
-        part[m * PP + row] = acc[r][mt][i];
-      }
+        for (int i = 0; i < 4; ++i) {
+          const int row = 16 * (RT * warp + r) + g + (i >= 2 ? 8 : 0), m = 8 * mt + 2 * t + (i & 1);
+          part[m * PP + row] = acc[r][mt][i];
+        }
+  }
   if (S == 1) {
     __syncthreads();
     for (int e = threadIdx.x; e < M * ROWS; e += kMmaThreads) {
