@@ -15,6 +15,10 @@ by time.
   e2e     the same metric through the public API (lowbit.ops.linear), eager, with each step's activations copied
           from pinned host memory to the GPU (one copy) and its outputs copied back (one copy) inside the timed
           region, the stream synchronized at the end of every step;
+  e2e_graph
+          the same public calls captured once in a CUDA graph (as a decode loop captures its step) and replayed
+          every step between the same two copies and synchronize: the host cost of eager calls (one CUDA launch,
+          ~2.5 us on the B200 hosts, per call) taken out;
   cpu_baseline / --impl reference
           the reference's CPU path (dequantize on CPU tensors + fp32 F.linear, lowbit/ops.py:119-123) restated in
           oracle/oracle.py, timed on the host cores of this machine.
@@ -568,6 +572,33 @@ def run_ours(args, rank, world, local):
         e2e_ms = float(t.item())
     e2e_val = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
+    # e2e_graph: the same public calls captured once per weight set in a CUDA graph (what a decode loop does with
+    # its step), replayed every step between the same host-to-device and device-to-host copies and a synchronize
+    eg = [capture(lambda layer=layer: [ops.linear(xv, wq, out=yv) for xv, yv, wq in zip(x_views, y_views, layer)])[0]
+          for layer in sets]
+
+    def eg_step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        eg[i % n_sets].replay()
+        y_host.copy_(y_dev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for i in range(3):
+        eg_step(i)
+    if dist:
+        dist.barrier()
+    ea.record(st)
+    for i in range(e2e_steps):
+        eg_step(i)
+    eb.record(st)
+    eb.synchronize()
+    eg_ms = ea.elapsed_time(eb)
+    if dist:
+        t = torch.tensor([eg_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        eg_ms = float(t.item())
+    e2e_graph_val = world * step_bytes * e2e_steps / (eg_ms * 1e-3) / 1e9
+    del eg
+
     # the other configurations, measured after the timed sweep in the same run: the single-GPU kernel legs
     # (per-shape M = 1, config 2, prefill dequantize) at one GPU; the decoders at every N (config 3 as replicas,
     # config 4 sharded over all ranks)
@@ -641,6 +672,11 @@ def run_ours(args, rank, world, local):
                 "how": "lowbit.ops.linear eager per call (out= slices of one device buffer); the step's 21 "
                        "activation rows pinned-host -> GPU in one copy and its 21 outputs -> pinned host in one "
                        "copy inside the timed region; stream synchronized at the end of each step"},
+        "e2e_graph": {"value": round(e2e_graph_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                      "how": "the same 21 lowbit.ops.linear calls captured once per weight set in a CUDA graph "
+                             "(as a decode loop captures its step) and replayed each step between the same "
+                             "pinned-host copies in and out; stream synchronized at the end of each step"},
         "gpu_launches": launches_per_step * args.steps,
     }
     line.update({k: v for k, v in extras.items() if v is not None})
