@@ -16,9 +16,9 @@ by time.
           from pinned host memory to the GPU (one copy) and its outputs copied back (one copy) inside the timed
           region, the stream synchronized at the end of every step;
   e2e_graph
-          the same public calls captured once in a CUDA graph (as a decode loop captures its step) and replayed
-          every step between the same two copies and synchronize: the host cost of eager calls (one CUDA launch,
-          ~2.5 us on the B200 hosts, per call) taken out;
+          the same step -- both copies and the public calls -- captured once in a CUDA graph, as a decode loop
+          captures its step, and replayed every step with a synchronize: the host cost of eager calls (one CUDA
+          launch, ~2.5 us on the B200 hosts, per call) taken out;
   cpu_baseline / --impl reference
           the reference's CPU path (dequantize on CPU tensors + fp32 F.linear, lowbit/ops.py:119-123) restated in
           oracle/oracle.py, timed on the host cores of this machine.
@@ -572,15 +572,18 @@ def run_ours(args, rank, world, local):
         e2e_ms = float(t.item())
     e2e_val = world * step_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
-    # e2e_graph: the same public calls captured once per weight set in a CUDA graph (what a decode loop does with
-    # its step), replayed every step between the same host-to-device and device-to-host copies and a synchronize
-    eg = [capture(lambda layer=layer: [ops.linear(xv, wq, out=yv) for xv, yv, wq in zip(x_views, y_views, layer)])[0]
-          for layer in sets]
+    # e2e_graph: the step as a decode loop runs it -- the pinned-host input copy, the same public calls and the
+    # copy of the outputs back to pinned host memory captured once per weight set in a CUDA graph -- replayed every
+    # step, then a synchronize
+    def eg_body(layer):
+        x_dev.copy_(x_host, non_blocking=True)
+        for xv, yv, wq in zip(x_views, y_views, layer):
+            ops.linear(xv, wq, out=yv)
+        y_host.copy_(y_dev, non_blocking=True)
+    eg = [capture(lambda layer=layer: eg_body(layer))[0] for layer in sets]
 
     def eg_step(i):
-        x_dev.copy_(x_host, non_blocking=True)
         eg[i % n_sets].replay()
-        y_host.copy_(y_dev, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     for i in range(3):
         eg_step(i)
@@ -674,9 +677,10 @@ def run_ours(args, rank, world, local):
                        "copy inside the timed region; stream synchronized at the end of each step"},
         "e2e_graph": {"value": round(e2e_graph_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                       "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                      "how": "the same 21 lowbit.ops.linear calls captured once per weight set in a CUDA graph "
-                             "(as a decode loop captures its step) and replayed each step between the same "
-                             "pinned-host copies in and out; stream synchronized at the end of each step"},
+                      "how": "the step captured once per weight set in a CUDA graph, as a decode loop captures "
+                             "its step: the pinned-host copy of the 21 activation rows, the same 21 "
+                             "lowbit.ops.linear calls, the copy of the 21 outputs to pinned host memory; each step "
+                             "replays the graph (both copies included) and synchronizes the stream"},
         "gpu_launches": launches_per_step * args.steps,
     }
     line.update({k: v for k, v in extras.items() if v is not None})
