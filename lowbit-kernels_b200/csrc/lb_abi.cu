@@ -178,8 +178,9 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                    (int)(group / 128)};
   p.bias = static_cast<const __half*>(bias);
   const int kernel = g_opt[LB_OPT_GEMV_KERNEL].load();
-  // The skinny mma.sync GEMM from 17 rows, and from 9 rows on layers of 8M+ weights or K < 512 (there, measured
-  // on B200, 1.2-2.4x faster than the one-shot GEMV's 16-row CTAs, which each re-read every activation row); the
+  // The skinny mma.sync GEMM from 17 rows; from 9 rows on layers of 8M+ weights or K < 512, and from 13 rows on
+  // layers of 2048+ rows (there, measured on B200, 1.1-2.4x faster than the one-shot GEMV's 16-row CTAs, which
+  // each re-read every activation row); the
   // tcgen05 GEMM above 48 rows on layers of more than 4.2M weights, where it measured up to 12 % faster (the
   // tensor-core pipe, not the weight stream, bounds the mma.sync kernel there).
   const bool tc_rows = m > 48 && n * k > 4200000;
@@ -189,7 +190,8 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
     if (splits > 0)
       return launched(lb::launch_gemm_tc05(p, splits, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm_tc");
   }
-  if (kernel == 5 || (kernel == 0 && (m > 16 || (m > 8 && (n * k >= (int64_t)1 << 23 || k < 512))))) {
+  if (kernel == 5 ||
+      (kernel == 0 && (m > 16 || (m > 8 && (n * k >= (int64_t)1 << 23 || k < 512 || (m > 12 && n >= 2048)))))) {
     // mma.sync tiles fed by tensor copies: CTAs of 64 weight rows sharing each activation chunk, clusters splitting K
     const lb::MmaConfig c = lb::gemm_mma_config((int)m, (int)n, (int)k, (int)group,
                                                 g_opt[LB_OPT_GEMV_KSPLIT].load(), g_opt[LB_OPT_GEMV_ROWTILES].load());
