@@ -50,9 +50,9 @@ typedef enum lb_option {
                                in the stream (only for weights no in-flight kernel writes); default 0 */
   LB_OPT_GEMV_KSPLIT = 2,   /* 0 (default): automatic; 1..8 forces the GEMV's K-split cluster size */
   LB_OPT_GEMV_WARPS = 3,    /* 0 (default): automatic; 4, 8 or 16 forces the GEMV's warps per CTA */
-  LB_OPT_GEMV_DEPTH = 4,    /* 0 (default): automatic; 4 or 8 forces the GEMV's copy-ring depth per warp */
-  LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 forces the persistent copy-ring GEMV, 2 the tcgen05
-                               GEMM (any M <= 64), 3 the one-shot GEMV with activations staged per CTA (the
+  LB_OPT_GEMV_DEPTH = 4,    /* reserved: no effect (the copy-ring GEMV it tuned was removed) */
+  LB_OPT_GEMV_KERNEL = 5,   /* 0 (default): automatic; 1 reserved (it forced a copy-ring GEMV, since removed),
+                               2 the tcgen05 GEMM (any M <= 64), 3 the one-shot GEMV with activations staged per CTA (the
                                automatic choice at M <= 8 stages them per warp, with the same bits), 4 the
                                M <= 8 GEMV with each weight tile landed in shared memory by one bulk copy, 5 the
                                skinny GEMM on mma.sync tiles fed by tensor copies (any M <= 64; the automatic

@@ -71,49 +71,6 @@ int check_common(const void* x, const void* w, const void* s, const void* y, int
   return LB_OK;
 }
 
-// GEMV tiling. Persistent CTAs walk 16-row tiles; the warps of a CTA split each tile's 128-wide chunks; a
-// cluster of S CTAs splits K further. A configuration is (warps NW, split S); CTAs per SM follow from NW
-// (16 resident warps per SM) and shared memory. The model: an SM's time is the bytes its busiest CTA slot
-// streams -- ceil(tiles / clusters) tiles of nl = ceil(KC / S) chunks -- times the CTAs sharing the SM,
-// with idle warps (nl not a multiple of NW) counted as if busy and a small charge per cluster split.
-lb::GemvConfig gemv_config(int M, int N, int K) {
-  lb::GemvConfig best{};
-  best.mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
-  best.pdl = g_opt[LB_OPT_PDL].load();
-  const int sms = g_sm_count > 0 ? g_sm_count : 148;
-  const int nt = (N + 15) / 16, kc = K >> 7;
-  const int forced_s = g_opt[LB_OPT_GEMV_KSPLIT].load(), forced_w = g_opt[LB_OPT_GEMV_WARPS].load();
-  const int forced_d = g_opt[LB_OPT_GEMV_DEPTH].load();
-  best.depth = forced_d == 4 || forced_d == 8 ? forced_d : 8;
-  double best_cost = 1e30;
-  for (int nw : {16, 8, 4}) {
-    if (best.mt >= 4 && nw == 16) continue;
-    if (forced_w && nw != forced_w) continue;
-    for (int s = 1; s <= 8 && s <= kc; ++s) {
-      if (forced_s && s != forced_s) continue;
-      const size_t smem = lb::gemv_smem_bytes(M, K, s, best.mt, nw, best.depth);
-      if (smem > 227 * 1024) continue;
-      int per_sm = 16 / nw;
-      while (per_sm > 1 && (size_t)per_sm * smem > 220 * 1024) --per_sm;
-      int clusters = sms * per_sm / s;
-      if (clusters > nt) clusters = nt;
-      if (clusters < 1) clusters = 1;
-      const int nl = (kc + s - 1) / s;
-      const int cpw = (nl + nw - 1) / nw;
-      const double tiles_per = (double)((nt + clusters - 1) / clusters);
-      const double ctas_on_sm = (double)(((long)clusters * s + sms - 1) / sms);
-      double cost = ctas_on_sm * tiles_per * (double)(cpw * nw) * (1.0 + 0.08 * (s > 1)) + 2.0 * tiles_per;
-      if (cost < best_cost) {
-        best_cost = cost;
-        best.warps = nw;
-        best.ksplit = s;
-        best.clusters = clusters;
-      }
-    }
-  }
-  return best;
-}
-
 // One-shot GEMV tiling, from a B200 sweep of the Qwen2.5 projections at M = 1 (every K-split 1..8, row tiles
 // 1..2, warps 2..16): splitting K across a cluster never paid (its two cluster barriers cost more than the
 // extra parallelism), one 16-row tile per CTA was best or within noise, and the post-wait critical path is
@@ -197,7 +154,7 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
                                                 g_opt[LB_OPT_GEMV_KSPLIT].load(), g_opt[LB_OPT_GEMV_ROWTILES].load());
     if (c.splits > 0) return launched(lb::launch_gemm_mma(p, c, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm");
   }
-  if (kernel != 1 && m <= 16) {
+  if (m <= 16) {
     const lb::OneshotConfig c = oneshot_config((int)m, (int)n, (int)k);
     if (c.warps > 0) {
       // the same tiling through the kernel that stages activations per warp (same bits) where it applies and, from
@@ -212,19 +169,12 @@ int run_gemv_mma(const void* x, const void* w, const void* s, void* y, int64_t m
       return launched(lb::launch_gemv_oneshot(p, c, st), "w4_gemv");
     }
   }
-  lb::GemvConfig c = gemv_config((int)m, (int)n, (int)k);
-  if (c.warps == 0) {
-    // the staged activations do not fit in shared memory: run the rows in two halves (each reads W once)
-    if (m == 1)
-      return fail(LB_ERR_ARGUMENT, "K=%lld is too long for %lld activation rows", (long long)k, (long long)m);
-    const int64_t h = (m / 2 + 7) & ~7LL;   // keep the first half a whole number of 8-row tiles
-    const int64_t m0 = h < m ? h : m / 2;
-    int rc = run_gemv_mma(x, w, s, y, m0, n, k, group, st, bias);
-    if (rc) return rc;
-    return run_gemv_mma(static_cast<const char*>(x) + m0 * k * 2, w, s, static_cast<char*>(y) + m0 * n * 2, m - m0,
-                        n, k, group, st, bias);
-  }
-  return launched(lb::launch_gemv_mma(p, c, st), "w4_gemv");
+  // what the kernels above do not take (the one-shot GEMV's staged activations would not fit shared memory at this
+  // K, or kernel 3 / 4 forced past 8 rows): the skinny GEMM, whose shared memory does not grow with K
+  const lb::MmaConfig c = lb::gemm_mma_config((int)m, (int)n, (int)k, (int)group, g_opt[LB_OPT_GEMV_KSPLIT].load(),
+                                              g_opt[LB_OPT_GEMV_ROWTILES].load());
+  if (c.splits == 0) return fail(LB_ERR_ARGUMENT, "no GEMV kernel takes M=%lld K=%lld", (long long)m, (long long)k);
+  return launched(lb::launch_gemm_mma(p, c, g_opt[LB_OPT_PDL].load() != 0, st), "w4_gemm");
 }
 
 }  // namespace

@@ -35,220 +35,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-struct GemvLayout {  // byte offsets inside dynamic shared memory
-  int x, ring, red, part, total;
-};
-
-__host__ __device__ inline GemvLayout gemv_layout(int M, int nl, int mt, int nw, int depth, int nsplit) {
-  GemvLayout L;
-  L.x = 0;
-  L.ring = ((M * gemv_x_row_words(nl) * 4) + 127) & ~127;
-  L.red = L.ring + nw * depth * 1024;
-  L.part = L.red + 2 * nw * mt * 512;
-  L.total = L.part + (nsplit > 1 ? 2 * nsplit * mt * 512 : 0);
-  return L;
-}
-
-template <int MT, int NW, int D>
-__global__ void __launch_bounds__(NW * 32) gemv_stream_kernel(GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int K = p.K, N = p.N, M = p.M;
-  const int KC = K >> 7, KG = K / p.G, cpg = p.G >> 7;
-  const int split = blockIdx.y, nsplit = gridDim.y;
-  const int c_begin = (int)((int64_t)KC * split / nsplit);
-  const int c_end = (int)((int64_t)KC * (split + 1) / nsplit);
-  const int nl = c_end - c_begin;
-  const int row_words = gemv_x_row_words(nl);
-  // the layout follows the largest rank's chunk count, so every rank of a cluster agrees on where rank 0's
-  // partial-sum buffer lives
-  const GemvLayout L = gemv_layout(M, (KC + nsplit - 1) / nsplit, MT, NW, D, nsplit);
-  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + L.x);
-  float* red = reinterpret_cast<float*>(smem + L.red);
-  float* part = reinterpret_cast<float*>(smem + L.part);
-  const uint32_t ring = smem_u32(smem + L.ring) + warp * (D * 1024) + lane * 16;   // + (slot * 2 + h) * 512
-
-  // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...; every warp walks the same job sequence:
-  // job = (tile iteration, slot ci < cpw) -> chunk c_begin + warp + NW * ci. Positions advance by counters
-  // (no integer division in the loop).
-  const int NT = (N + 15) >> 4;
-  const int ntiles = blockIdx.x < NT ? (NT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int cpw = (nl + NW - 1) / NW;
-  const int J = ntiles * cpw;
-  const uint4* w4 = reinterpret_cast<const uint4*>(p.w);
-  const uint16_t* s16 = reinterpret_cast<const uint16_t*>(p.s);
-  const size_t row_stride = (size_t)(K >> 5);   // uint4 per row
-  const int c_warp = c_begin + warp;
-
-  struct Cursor {   // a job position: tile iteration and slot
-    int it, ci;
-    __device__ void next(int cpw_) {
-      if (++ci == cpw_) { ci = 0; ++it; }
-    }
-  };
-
-  uint16_t sra[D], srb[D];
-  Cursor iss{0, 0};   // next job to issue
-  // start the copies of the job at `iss` into ring slot `slot` and its scales into ra_s/rb_s; always one group
-  auto issue = [&](int slot, uint16_t& ra_s, uint16_t& rb_s) {
-    if (iss.it < ntiles) {
-      const int c = c_warp + NW * iss.ci;
-      if (c < c_end) {
-        const int n0 = (blockIdx.x + gridDim.x * iss.it) * 16;
-        const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);   // tail rows re-read row N-1
-        cp_async16(ring + (slot * 2 + 0) * 512, w4 + (size_t)ra * row_stride + 4 * c + t);
-        cp_async16(ring + (slot * 2 + 1) * 512, w4 + (size_t)rb * row_stride + 4 * c + t);
-        const int grp = cpg == 1 ? c : c / cpg;
-        ra_s = ldg_u16(s16 + (size_t)ra * KG + grp);
-        rb_s = ldg_u16(s16 + (size_t)rb * KG + grp);
-      }
-    }
-    cp_async_commit();
-    iss.next(cpw);
-  };
-
-  pdl_launch_dependents();
-  const bool early = (p.flags & kFlagEarlyWeights) != 0;
-  if (!early) pdl_wait();
-#pragma unroll
-  for (int u = 0; u < D - 1; ++u) issue(u, sra[u], srb[u]);
-  if (early) pdl_wait_after_loads(p.wait_guard);
-
-  // stage x[:, chunks c_begin..c_end) in consumption order: word (m * row_words + lc * 64 + qd * 16 + t * 4 + e)
-  // holds the pair x[m][128 c + 8 s + 2 t .. +1] with s = 4 qd + e
-  {
-    const uint32_t* xw = reinterpret_cast<const uint32_t*>(p.x) + (size_t)c_begin * 64;
-    const int pairs = nl * 64;
-    for (int m = 0; m < M; ++m) {
-      for (int pi = threadIdx.x; pi < pairs; pi += NW * 32) {
-        const int lc = pi >> 6, o = pi & 63, s = o >> 2, tt = o & 3;
-        xs[m * row_words + lc * 64 + (s >> 2) * 16 + tt * 4 + (s & 3)] = ldg_cg_u32(xw + (size_t)m * (K >> 1) + pi);
-      }
-    }
-  }
-  __syncthreads();
-
-  int xoff[MT];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) xoff[mt] = min(8 * mt + g, M - 1) * row_words + t * 4;
-
-  float acc[MT][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
-
-  constexpr int kTile = MT * 128;
-  int buf = 0;
-  Cursor cur{0, 0};   // job being computed
-
-  // end of a tile: publish the warps' partial sums, reduce in one warp, store (or hand to the cluster's rank 0)
-  auto tile_end = [&](int it, int& b, float (&a)[MT][4]) {
-    const int n0 = (blockIdx.x + gridDim.x * it) * 16;
-    float* rb = red + b * NW * kTile;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        rb[(warp * MT + mt) * 128 + i * 32 + lane] = a[mt][i];
-        a[mt][i] = 0.f;
-      }
-    __syncthreads();
-    const bool reducer = warp == (it & (NW - 1));
-    auto store = [&](int e, float v) {
-      const int mt = e >> 7, i = (e >> 5) & 3, ln = e & 31;
-      const int row = n0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-      const int m = 8 * mt + 2 * (ln & 3) + (i & 1);
-      if (row < N && m < M) p.y[(size_t)m * N + row] = out_half(v, p.bias, row);
-    };
-    if (nsplit == 1) {
-      if (reducer) {
-#pragma unroll
-        for (int e = lane; e < kTile; e += 32) {
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
-          store(e, v);
-        }
-      }
-    } else {
-      cg::cluster_group cluster = cg::this_cluster();
-      float* pb = part + b * nsplit * kTile;
-      if (reducer) {
-        float* dst = cluster.map_shared_rank(pb, 0) + split * kTile;
-#pragma unroll
-        for (int e = lane; e < kTile; e += 32) {
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < NW; ++w) v += rb[w * kTile + e];
-          dst[e] = v;
-        }
-      }
-      cluster.sync();
-      if (split == 0 && reducer) {
-        for (int e = lane; e < kTile; e += 32) {
-          float v = 0.f;
-          for (int r = 0; r < nsplit; ++r) v += pb[r * kTile + e];
-          store(e, v);
-        }
-      }
-    }
-    b ^= 1;
-  };
-  const uint8_t* ring_ptr = smem + (ring - smem_u32(smem));
-
-  for (int j0 = 0; j0 < J; j0 += D) {
-#pragma unroll
-    for (int u = 0; u < D; ++u) {
-      issue((u + D - 1) % D, sra[(u + D - 1) % D], srb[(u + D - 1) % D]);
-      cp_async_wait<D - 1>();   // the group of this job has landed (this lane's own copies)
-      if (cur.it < ntiles) {
-        const int c = c_warp + NW * cur.ci;
-        if (c < c_end) {
-          const int lc = c - c_begin;
-          const uint4 qa = *reinterpret_cast<const uint4*>(ring_ptr + (u * 2 + 0) * 512);
-          const uint4 qb = *reinterpret_cast<const uint4*>(ring_ptr + (u * 2 + 1) * 512);
-          float d[MT][4];
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) d[mt][i] = 0.f;
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            uint32_t w0 = (&qa.x)[qd], w1 = (&qb.x)[qd];
-            uint4 xb[MT];
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-              xb[mt] = *reinterpret_cast<const uint4*>(xs + xoff[mt] + lc * 64 + qd * 16);
-            // k16 step 2qd: pairs 0 (k = .. + 2t) and 1 (k = .. + 8 + 2t)
-            uint32_t f0 = q_pair_lo(w0), f1 = q_pair_lo(w1), f2 = q_pair_hi(w0), f3 = q_pair_hi(w1);
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].x, xb[mt].y);
-            // k16 step 2qd + 1: pairs 2 and 3, the same extraction on the word shifted by 8
-            w0 >>= 8;
-            w1 >>= 8;
-            f0 = q_pair_lo(w0); f1 = q_pair_lo(w1); f2 = q_pair_hi(w0); f3 = q_pair_hi(w1);
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma16816(d[mt], f0, f1, f2, f3, xb[mt].z, xb[mt].w);
-          }
-          const float s0 = h2f_bits(sra[u]), s1 = h2f_bits(srb[u]);
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            acc[mt][0] = fmaf(s0, d[mt][0], acc[mt][0]);
-            acc[mt][1] = fmaf(s0, d[mt][1], acc[mt][1]);
-            acc[mt][2] = fmaf(s1, d[mt][2], acc[mt][2]);
-            acc[mt][3] = fmaf(s1, d[mt][3], acc[mt][3]);
-          }
-        }
-        if (cur.ci == cpw - 1) tile_end(cur.it, buf, acc);
-      }
-      cur.next(cpw);
-    }
-  }
-  cp_async_wait<0>();
-  if (nsplit > 1) cg::this_cluster().sync();   // rank 0's buffers stay alive until every rank is done with them
-}
-
 // One-shot GEMV (M <= 16), the decode path. One CTA owns RT 16-row tiles and a K range (a cluster of S
 // CTAs splits long K); its warps split the range's chunks, at most CPW each. At entry every thread issues
 // ALL of its weight and scale loads (register destinations, L1 bypassed) -- ahead of the wait on the previous
@@ -1242,55 +1028,6 @@ __global__ void __launch_bounds__(128) gemv_compat_kernel(GemvParams p) {
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
-
-template <int MT, int NW, int D>
-static cudaError_t launch_stream(const GemvParams& p, const GemvConfig& c, cudaStream_t st) {
-  const int KC = p.K >> 7;
-  const int max_nl = (KC + c.ksplit - 1) / c.ksplit;
-  const GemvLayout L = gemv_layout(p.M, max_nl, MT, NW, D, c.ksplit);
-  auto kern = gemv_stream_kernel<MT, NW, D>;
-  if (L.total > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
-    if (e != cudaSuccess) return e;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(c.clusters, c.ksplit, 1);
-  cfg.blockDim = dim3(NW * 32, 1, 1);
-  cfg.dynamicSmemBytes = L.total;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (c.ksplit > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = c.ksplit;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  if (c.pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
-size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth) {
-  const int KC = K >> 7, max_nl = (KC + nsplit - 1) / nsplit;
-  return (size_t)gemv_layout(M, max_nl, mt, nw, depth, nsplit).total;
-}
-
-cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st) {
-#define LB_STREAM(MT_, NW_)                                                              \
-  if (c.mt == MT_ && c.warps == NW_)                                                     \
-    return c.depth == 8 ? launch_stream<MT_, NW_, 8>(p, c, st) : launch_stream<MT_, NW_, 4>(p, c, st);
-  LB_STREAM(1, 4) LB_STREAM(1, 8) LB_STREAM(1, 16) LB_STREAM(2, 4) LB_STREAM(2, 8) LB_STREAM(2, 16)
-  LB_STREAM(4, 4) LB_STREAM(4, 8) LB_STREAM(8, 4) LB_STREAM(8, 8)
-#undef LB_STREAM
-  return cudaErrorInvalidConfiguration;
-}
 
 template <int M, int R, bool V3>
 static cudaError_t launch_compat_t(const GemvParams& p, cudaStream_t st, bool pdl) {

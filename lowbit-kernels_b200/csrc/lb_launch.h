@@ -51,17 +51,6 @@ struct GemvParams {
   int ar_rank = 0, ar_world = 1, ar_cap = 0;
 };
 
-struct GemvConfig {
-  int mt;        // n8 activation tiles (1: M <= 8, 2: M <= 16, 4: M <= 32, 8: M <= 64)
-  int warps;     // warps per CTA (4, 8 or 16)
-  int ksplit;    // CTAs per cluster splitting K (1..8)
-  int clusters;  // persistent CTA groups (grid.x); each walks 16-row tiles x, x + clusters, ...
-  int depth;     // cp.async ring depth per warp (chunks in flight): 4 or 8
-  int pdl;       // launch with programmatic stream serialization
-};
-
-cudaError_t launch_gemv_mma(const GemvParams& p, const GemvConfig& c, cudaStream_t st);
-
 // one-shot GEMV (M <= 16): one 16-row tile per CTA, all weight loads issued at entry
 struct OneshotConfig {
   int warps;   // warps per CTA (1..16)
@@ -83,7 +72,6 @@ size_t bulk_smem_bytes(int M, int K, int nw, int cpw);
 // device status word (lb_gemv.cu): nonzero after a bounded wait in a kernel gave up
 int device_error();   // synchronizes
 void clear_device_error();
-size_t gemv_smem_bytes(int M, int K, int nsplit, int mt, int nw, int depth);
 cudaError_t launch_gemv_compat(const GemvParams& p, int rows_per_warp, bool v3, bool pdl, cudaStream_t st);
 
 // format kernels (lb_format.cu)
