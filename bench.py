@@ -1031,6 +1031,64 @@ def fuse_arg(args, config=None):
     return tuple(x for x in f.split(",") if x)
 
 
+def tp_timeline(args, rank, world, local, steps=16):
+    """No headline: where the time of one config-4 decode step goes at this world size. The step graph is replayed
+    `steps` times under torch's CUPTI profiler on every rank; rank 0 prints one JSON line with each kernel's GPU
+    time per step and share, plus the graph-timed step. A kernel that waits on its peers (the fused GEMV +
+    allreduce, the one-shot allreduce, NCCL) is charged its waiting time, so the table names the collective or
+    kernel that bounds the tensor-parallel step. Kernels overlap under programmatic dependent launch, so the
+    per-kernel times add up to more than the step."""
+    from torch.profiler import ProfilerActivity, profile
+    from lowbit import decode
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_dist(device) if world > 1 else None
+    decode.enable_decode_options()
+    allreduce = getattr(args, "allreduce", "oneshot")
+    m = decode.build(decode.QWEN25_7B, seed=0, device=device)
+    dec = decode.Int4Decoder(m, TP_CONTEXT + 3 * steps + 16, world=world, rank=rank,
+                             pg=dist.group.WORLD if dist else None, allreduce=allreduce, fuse=fuse_arg(args, 4))
+    del m
+    torch.cuda.empty_cache()
+    prompt = torch.randint(0, decode.QWEN25_7B["vocab_size"], (TP_CONTEXT,), generator=torch.Generator().manual_seed(7))
+    dec.prefill(prompt)
+    for _ in range(steps):
+        dec.step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        dec.step()
+    b.record()
+    b.synchronize()
+    step_us = a.elapsed_time(b) * 1e3 / steps
+    if dist:
+        dist.barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            dec.step()
+        torch.cuda.synchronize()
+    kern = {}
+    for ev in prof.key_averages():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and ev.count:
+            k = kern.setdefault(ev.key[:90], [0, 0.0])
+            k[0] += ev.count
+            k[1] += ev.device_time_total
+    total = sum(v[1] for v in kern.values()) or 1.0
+    rows = sorted(kern.items(), key=lambda kv: -kv[1][1])
+    line = {"tp_timeline": world, "fuse": list(fuse_arg(args, 4)), "allreduce": allreduce,
+            "step_us_graph": round(step_us, 1), "kernel_us_per_step": round(total / steps, 1),
+            "kernels": [{"kernel": k, "launches_per_step": round(c / steps, 2), "us_per_step": round(t / steps, 1),
+                         "share": round(t / total, 3)} for k, (c, t) in rows[:25]]}
+    if dist:
+        dist.barrier()
+        del dec
+        dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
 def profile_decode(fuse=(), steps=3, prompt_len=8):
     """No timing: the config-3 decoder (Qwen2.5-3B, INT4) with a short prompt, then a few graph steps, for an ncu
     launch list of whole decode steps."""
@@ -1070,6 +1128,8 @@ def main():
                     help="sweep the config-1 shapes at M = 1..256 and write the record the dispatch table follows from")
     ap.add_argument("--profile-decode", action="store_true", help="no timing: a few config-3 decode steps, for ncu")
     ap.add_argument("--profile-sweep", action="store_true", help="no timing: two cold passes over the config-1 calls")
+    ap.add_argument("--tp-timeline", action="store_true",
+                    help="no headline: per-kernel GPU time of one config-4 decode step at this world size (CUPTI)")
     ap.add_argument("--profile-case", default=None, metavar="K,N,M",
                     help="no timing: a few launches of one GEMV shape, for a small ncu capture")
     args = ap.parse_args()
@@ -1090,7 +1150,9 @@ def main():
     rank, world, local = rank_env()
     if world != args.gpus and world > 1:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
-    if args.impl == "reference":
+    if args.tp_timeline:
+        line = tp_timeline(args, rank, world, local)
+    elif args.impl == "reference":
         line = run_reference(args, rank, world)
     elif args.config == 3:
         line = run_decode(args, rank, world, local)

@@ -176,7 +176,7 @@ def test_every_gemv_kernel(layers, kernel, name, m):
     finally:
         e.set_option("gemv_kernel", prev)
     y64 = ref_y(x, packed, scales, 128)
-    if kernel == 2 or (kernel in (0, 5) and m > 16):
+    if kernel == 2 or m > 16:   # above 16 rows every path multiplies fp16-rounded weights
         check_gemm_output(y, y64, x, packed, scales, 128, f"kernel {kernel} {name} M={m}")
     else:
         check_output(y, y64, f"kernel {kernel} {name} M={m}")
