@@ -929,7 +929,7 @@ def run_tp_decode(args, rank, world, local, dist=None, steps=None, warm=None):
     decode.enable_decode_options()
     steps = steps or min(args.steps, 256)
     warm = warm or min(args.warmup, 64)
-    fuse = fuse_arg(args, 4)
+    fuse = fuse_arg(args, 4, world)
     allreduce = getattr(args, "allreduce", "oneshot")
     m = decode.build(decode.QWEN25_7B, seed=0, device=device)
     dec = decode.Int4Decoder(m, TP_CONTEXT + warm + steps + 16, world=world, rank=rank,
@@ -1019,15 +1019,20 @@ def profile_sweep(passes=2):
 
 # measured defaults (B200): config 3 runs fastest with the separate kernels; config 4 with the o and down GEMVs
 # fused with their allreduce, residual add and RMSNorm (TP2 488 tok/s against 474 for GEMV then allreduce + norm)
-DEFAULT_FUSE = {3: "", 4: "epilogue,gemv_allreduce"}
+DEFAULT_FUSE = {3: "", 4: "epilogue"}
+# config 4 at two ranks: the o and down GEMVs also fused with their allreduce (measured at TP2: 610 against 543
+# tok/s); at eight the fused kernel's last CTA, polling every rank's region, made the step slower than separate
+# GEMV + one-shot allreduce kernels (3121 against 1921 us per token, `--tp-timeline`)
+DEFAULT_FUSE_TP2 = "epilogue,gemv_allreduce"
 
 
-def fuse_arg(args, config=None):
+def fuse_arg(args, config=None, world=1):
     """--fuse: comma-separated kernel fusions of the decode step (Int4Decoder's `fuse`); the config's measured
-    default when not given."""
+    default at this world size when not given."""
     f = getattr(args, "fuse", None)
     if f is None:
-        f = DEFAULT_FUSE.get(config or getattr(args, "config", 3), "")
+        cfg = config or getattr(args, "config", 3)
+        f = DEFAULT_FUSE_TP2 if cfg == 4 and world == 2 else DEFAULT_FUSE.get(cfg, "")
     return tuple(x for x in f.split(",") if x)
 
 
@@ -1047,7 +1052,7 @@ def tp_timeline(args, rank, world, local, steps=16):
     allreduce = getattr(args, "allreduce", "oneshot")
     m = decode.build(decode.QWEN25_7B, seed=0, device=device)
     dec = decode.Int4Decoder(m, TP_CONTEXT + 3 * steps + 16, world=world, rank=rank,
-                             pg=dist.group.WORLD if dist else None, allreduce=allreduce, fuse=fuse_arg(args, 4))
+                             pg=dist.group.WORLD if dist else None, allreduce=allreduce, fuse=fuse_arg(args, 4, world))
     del m
     torch.cuda.empty_cache()
     prompt = torch.randint(0, decode.QWEN25_7B["vocab_size"], (TP_CONTEXT,), generator=torch.Generator().manual_seed(7))
@@ -1078,7 +1083,7 @@ def tp_timeline(args, rank, world, local, steps=16):
             k[1] += ev.device_time_total
     total = sum(v[1] for v in kern.values()) or 1.0
     rows = sorted(kern.items(), key=lambda kv: -kv[1][1])
-    line = {"tp_timeline": world, "fuse": list(fuse_arg(args, 4)), "allreduce": allreduce,
+    line = {"tp_timeline": world, "fuse": list(fuse_arg(args, 4, world)), "allreduce": allreduce,
             "step_us_graph": round(step_us, 1), "kernel_us_per_step": round(total / steps, 1),
             "kernels": [{"kernel": k, "launches_per_step": round(c / steps, 2), "us_per_step": round(t / steps, 1),
                          "share": round(t / total, 3)} for k, (c, t) in rows[:25]]}
